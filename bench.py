@@ -1,0 +1,378 @@
+"""Benchmark of the MXFP8 quantizer hot path (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one quantization of this rank's 8192 x 8192 bf16 N(0,1) matrix
+into E4M3 payload + packed UE8M0 scales.  Under torchrun
+with N ranks every rank quantizes its own 8192-row shard of a (8192*N) x 8192
+matrix (64 row chunks of 128 rows each): weak scaling, no collective on the
+data path; the timed region is bracketed by barriers and reported as the max
+over ranks.  Metric: effective TB/s = (2MK + MK + MK/32) bytes / device time,
+summed over ranks.
+
+Inputs rotate over enough workspaces (X, Q, S sets) that one rotation is more
+than three times the L2 size, so every step streams from HBM.
+
+``--impl reference`` times the reference recipe's CPU implementation (the
+integer-exact C restatement in oracle/, all host threads) on a bounded row
+sample of the same workload; rank 0 alone runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import pathlib
+import re
+import statistics
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+M_DEFAULT, K_DEFAULT = 8192, 8192
+METRIC = "effective TB/s (2MK+MK+MK/32 B / device time) at 8192x8192 bf16; % of HBM peak"
+SCALE_VEC = 32
+
+
+def algo_bytes(m: int, k: int) -> int:
+    return 2 * m * k + m * k + m * (k // SCALE_VEC)
+
+
+def measured_hbm_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic(m: int, k: int) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary, if any."""
+    for p in sorted((ROOT / "profiles").glob("*.md")) + sorted((ROOT / "profiles").glob("*.txt")):
+        mt = re.search(rf"traffic_bytes_per_launch\[{m}x{k}\]:\s*([0-9.eE+]+)", p.read_text())
+        if mt:
+            return float(mt.group(1))
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML during a region."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.nvml:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self) -> dict:
+        if self._thread:
+            self._stop.set()
+            self._thread.join()
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        seen = 0
+        for _, r in busy:
+            seen |= r
+        return {"sm_mhz": statistics.median(s[0] for s in busy), "sm_max_mhz": self.max_mhz,
+                "reasons": [name for bit, name in self.REASONS.items() if seen & bit and bit != 0x1],
+                "samples": len(busy)}
+
+
+def cpu_oracle_time(x_bits, m_rows: int, k: int, reps: int, threads: int) -> float:
+    import oracle  # test infrastructure: the CPU baseline only
+
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.quantize(x_bits[:m_rows], "bf16", m_rows, k, nthreads=threads)
+        best = min(best, time.perf_counter() - t0)
+    return best
+
+
+def host_workload(m: int, k: int, seed: int):
+    import numpy as np
+    import torch
+
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    return torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
+def base_line(args, world: int) -> dict:
+    return {
+        "metric": METRIC,
+        "unit": "TB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: N(0,1) bf16, seeded, generated on the device (no dataset involved)",
+        "config": {
+            "workload": f"{args.m}x{args.k} bf16 -> e4m3 + ue8m0 (tcgen05 128x4 chunks) per rank; "
+                        f"rank r owns rows [r*{args.m}, (r+1)*{args.m}) of a ({args.m}*N)x{args.k} matrix",
+            "m_per_rank": args.m, "k": args.k, "input_dtype": "bf16", "global_m": args.m * world,
+            "parallelism": f"row shards of 128-row chunks x{world}, no collective",
+        },
+    }
+
+
+def reference_arm(args, rank: int, world: int) -> None:
+    """CPU implementation of the recipe, rank 0 only."""
+    if rank != 0:
+        return
+    sys_path_oracle()
+    threads = os.cpu_count() or 1
+    x = host_workload(args.m, args.k, 1)
+    # size each step's row sample so the whole run stays within ~2 minutes
+    probe_rows = min(args.m, 1024)
+    t_probe = cpu_oracle_time(x, probe_rows, args.k, 1, threads)
+    per_row = t_probe / probe_rows
+    budget = min(0.5, 120.0 / max(1, args.steps + args.warmup))
+    rows = int(max(128, min(args.m, budget / max(per_row, 1e-9))) // 128 * 128)
+    for _ in range(args.warmup):
+        cpu_oracle_time(x, rows, args.k, 1, threads)
+    times = [cpu_oracle_time(x, rows, args.k, 1, threads) for _ in range(args.steps)]
+    total = sum(times)
+    value = algo_bytes(rows, args.k) * args.steps / total / 1e12
+    line = base_line(args, world)
+    sample = f"{rows}x{args.k} rows of the workload per step, {threads} threads, C restatement of the recipe"
+    line.update({
+        "impl": "reference",
+        "value": value,
+        "ms_per_step": total / args.steps * 1e3,
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    })
+    line["config"]["cpu"] = cpu_model()
+    print(json.dumps(line), flush=True)
+
+
+def cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def sys_path_oracle():
+    import sys
+
+    p = str(ROOT / "oracle")
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--m", type=int, default=M_DEFAULT)
+    ap.add_argument("--k", type=int, default=K_DEFAULT)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="kernel launches only (verify, warm-up, K launches): the command profiled with ncu")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import MXFP8_quantizer
+
+    pkg = MXFP8_quantizer.load_package()
+    capi = pkg._capi
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    m, k = args.m, args.k
+    nbytes = algo_bytes(m, k)
+    s_bytes = capi.scale_storage_bytes(m, k)
+    ws_bytes = 2 * m * k + m * k + s_bytes
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    n_ws = max(2, math.ceil(3 * l2 / ws_bytes))
+    gen = torch.Generator(device=dev).manual_seed(1 + rank)
+    xs = [torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16) for _ in range(n_ws)]
+    qs = [torch.empty((m, k), dtype=torch.uint8, device=dev) for _ in range(n_ws)]
+    ss = [torch.empty((s_bytes,), dtype=torch.uint8, device=dev) for _ in range(n_ws)]
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    lib = capi.lib()
+    launch_args = [(xs[i].data_ptr(), 0, m, k, k, qs[i].data_ptr(), m, k, k, ss[i].data_ptr(), s_bytes, sh)
+                   for i in range(n_ws)]
+
+    def launch(i):
+        rc = lib.mxfp8_quantize(*launch_args[i])
+        if rc:
+            capi.check(rc, "bench launch")
+
+    # correctness gate before timing (the reference does the same, MXFP8_quantizer.py:912-935)
+    launch(0)
+    torch.cuda.synchronize()
+    buffers = {"x": xs[0], "q_fp8": qs[0].view(torch.float8_e4m3fn), "s_storage_bytes": ss[0]}
+    ver = pkg.verify_quantizer_outputs(buffers, m, k, m, k)
+    if not ver["verification_passed"] or ver["q_max_byte_diff"] != 0:
+        raise SystemExit(f"verification failed on rank {rank}: {ver}")
+
+    for i in range(args.warmup):
+        launch(i % n_ws)
+    torch.cuda.synchronize()
+    if args.profile:
+        for i in range(args.steps):
+            launch(i % n_ws)
+        torch.cuda.synchronize()
+        if capi.device_status(clear=True):
+            raise SystemExit("device status word set")
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "m": m, "k": k, "launches": 1 + args.warmup + args.steps}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    sampler = ClockSampler(local)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    start.record(stream)
+    for i in range(args.steps):
+        launch(i % n_ws)
+    end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier()
+    elapsed_ms = start.elapsed_time(end)
+    status = capi.device_status(clear=True)
+    if status:
+        raise SystemExit(f"device status word {status:#x} after the timed region")
+    max_ms = max_over_ranks(elapsed_ms)
+    ms_per_step = max_ms / args.steps
+    value = world * nbytes / (ms_per_step * 1e-3) / 1e12
+
+    # kernel roofline: this rank's average launch over the timed region
+    peak, peak_kind = measured_hbm_peak()
+    achieved = nbytes / (elapsed_ms / args.steps * 1e-3) / 1e9
+    traffic = committed_traffic(m, k)
+
+    # end to end through the public API with host buffers: pinned X in, Q and S out
+    x_host = torch.empty((m, k), dtype=torch.bfloat16, pin_memory=True)
+    x_host.copy_(xs[0].cpu())
+    q_host = torch.empty((m, k), dtype=torch.uint8, pin_memory=True)
+    s_host = torch.empty((s_bytes,), dtype=torch.uint8, pin_memory=True)
+    hq = pkg.HostQuantizer(m, k, torch.bfloat16, device=dev)
+    for _ in range(2):
+        hq(x_host, q_host, s_host)
+    torch.cuda.synchronize()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e_start.record(stream)
+    for _ in range(args.e2e_steps):
+        hq(x_host, q_host, s_host)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end)) / args.e2e_steps
+    if not torch.equal(q_host, qs[0].cpu()) or not torch.equal(s_host, ss[0].cpu()):
+        raise SystemExit("end-to-end output differs from the device-resident result")
+    e2e_value = world * nbytes / (e2e_ms * 1e-3) / 1e12
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys_path_oracle()
+        threads = os.cpu_count() or 1
+        xb = x_host.view(torch.int16).numpy().view("uint16")
+        t_all = cpu_oracle_time(xb, m, k, 3, threads)
+        cpu = {"value": nbytes / t_all / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+               "sample": f"the full {m}x{k} workload, best of 3, C restatement of the recipe on {cpu_model()}"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = base_line(args, world)
+    line["config"]["l2"] = f"{n_ws} rotating workspaces of {ws_bytes / 1e6:.0f} MB (> 3x the {l2 / 1e6:.0f} MB L2)"
+    line.update({
+        "value": value,
+        "ms_per_step": ms_per_step,
+        "clocks": clocks,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": nbytes},
+        "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": 2 * m * k,
+                "d2h_bytes_per_step": m * k + s_bytes, "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps,
+        "verification": ver,
+    })
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,196 @@
+// capi.cu -- the extern "C" boundary of libmxfp8.so (declared in
+// include/mxfp8.h): argument validation, per-device state, kernel choice.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+
+#include "../../include/mxfp8.h"
+#include "launch.h"
+
+namespace mxfp8 {
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int64_t kInt32Max = 2147483647;
+
+struct DeviceState {
+    bool ready = false;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    unsigned int* status = nullptr;  // device error word (see mxfp8_device_status)
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+thread_local std::string g_last_error;
+
+// Lazily fills the state of the current device (allocates its status word
+// on first use).  Returns 0 or a negative status.
+int current_device(DeviceState** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_last_error("cudaGetDevice", (int)e);
+        return MXFP8_ERR_DEVICE;
+    }
+    std::lock_guard<std::mutex> lock(g_mu);
+    DeviceState& st = g_dev[dev];
+    if (!st.ready) {
+        cudaDeviceProp prop;
+        e = cudaGetDeviceProperties(&prop, dev);
+        if (e != cudaSuccess) {
+            set_last_error("cudaGetDeviceProperties", (int)e);
+            return MXFP8_ERR_DEVICE;
+        }
+        st.sm_count = prop.multiProcessorCount;
+        st.cc_major = prop.major;
+        st.cc_minor = prop.minor;
+        if (st.cc_major == 10 && st.cc_minor == 0) {
+            e = cudaMalloc(&st.status, 256);
+            if (e == cudaSuccess) e = cudaMemset(st.status, 0, 256);
+            if (e != cudaSuccess) {
+                set_last_error("status word allocation", (int)e);
+                st.status = nullptr;
+                return MXFP8_ERR_CUDA;
+            }
+        }
+        st.ready = true;
+    }
+    if (st.cc_major != 10 || st.cc_minor != 0) {
+        set_last_error("libmxfp8 is built for sm_100a (B200); the current device is another architecture", 0);
+        return MXFP8_ERR_DEVICE;
+    }
+    *out = &st;
+    return MXFP8_OK;
+}
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+void set_last_error(const char* what, int code) {
+    g_last_error = what;
+    if (code) {
+        g_last_error += ": ";
+        g_last_error += cudaGetErrorName(static_cast<cudaError_t>(code));
+        g_last_error += " (";
+        g_last_error += std::to_string(code);
+        g_last_error += ")";
+    }
+}
+
+}  // namespace mxfp8
+
+using namespace mxfp8;
+
+extern "C" MXFP8_API int64_t mxfp8_scale_storage_bytes(int64_t rows, int64_t cols) {
+    if (rows < 0 || cols < 0) return -1;
+    return ceil_div(rows, 128) * 128 * (ceil_div(ceil_div(cols, 32), 4) * 4);
+}
+
+extern "C" MXFP8_API int mxfp8_launch_shape(int64_t m, int64_t k, int64_t* kernel_m, int64_t* kernel_k) {
+    if (!kernel_m || !kernel_k) return MXFP8_ERR_NULL_POINTER;
+    if (m < 1 || k < 1 || m > kInt32Max || k > kInt32Max) return MXFP8_ERR_SHAPE;
+    const int64_t km = ceil_div(m, 8) * 8, kk = ceil_div(k, 256) * 256;
+    if (km / 8 > kInt32Max || kk / 256 > 65535) return MXFP8_ERR_SHAPE;
+    *kernel_m = km;
+    *kernel_k = kk;
+    return MXFP8_OK;
+}
+
+extern "C" MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int64_t k, int64_t ld_x, void* q,
+                              int64_t q_rows, int64_t q_cols, int64_t ld_q, void* s, int64_t s_bytes,
+                              mxfp8_stream_t stream) {
+    if (dtype != MXFP8_BF16 && dtype != MXFP8_FP16) return MXFP8_ERR_DTYPE;
+    if (m < 0 || k < 0 || q_rows < m || q_cols < k || q_cols % 32 != 0 || ld_x < k || ld_q < q_cols ||
+        q_rows > kInt32Max || q_cols > kInt32Max || ld_x > (int64_t(1) << 38) || ld_q > (int64_t(1) << 39))
+        return MXFP8_ERR_SHAPE;
+    if (q_rows == 0 || q_cols == 0) return MXFP8_OK;
+    const bool has_x = m > 0 && k > 0;
+    if (!q || !s || (has_x && !x)) return MXFP8_ERR_NULL_POINTER;
+    if ((has_x && !aligned(x, 2)) || !aligned(s, 4)) return MXFP8_ERR_ALIGNMENT;
+    if (s_bytes < mxfp8_scale_storage_bytes(q_rows, q_cols)) return MXFP8_ERR_SCALE_BUFFER;
+
+    QuantizeArgs a;
+    a.x = x;
+    a.dtype = dtype;
+    a.m = m;
+    a.k = k;
+    a.ld_x = ld_x;
+    a.q = static_cast<uint8_t*>(q);
+    a.q_rows = q_rows;
+    a.q_cols = q_cols;
+    a.ld_q = ld_q;
+    a.s = static_cast<uint8_t*>(s);
+    a.scale_rows = ceil_div(q_rows, 128) * 128;
+    a.scale_cols = q_cols / 32;
+    a.col_chunks = ceil_div(a.scale_cols, 4);
+    if ((a.scale_rows / 128) * a.col_chunks > kInt32Max) return MXFP8_ERR_SHAPE;
+
+    DeviceState* dev = nullptr;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    a.status = dev->status;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool tma_ok = has_x && aligned(x, 16) && ld_x % 8 == 0 && aligned(q, 16) && ld_q % 16 == 0 &&
+                        aligned(s, 16);
+    return tma_ok ? launch_quantize_tma(a, dev->sm_count, st) : launch_quantize_generic(a, dev->sm_count, st);
+}
+
+extern "C" MXFP8_API int mxfp8_quantize_padded(const void* x, void* q_dwords, void* s_words, int64_t m, int64_t k,
+                                     int64_t s_word_count, int dtype, mxfp8_stream_t stream) {
+    if (m < 1 || k < 1 || m % 8 != 0 || k % 256 != 0 || s_word_count < 0) return MXFP8_ERR_SHAPE;
+    if (!x || !q_dwords || !s_words) return MXFP8_ERR_NULL_POINTER;
+    return mxfp8_quantize(x, dtype, m, k, k, q_dwords, m, k, k, s_words, s_word_count * 4, stream);
+}
+
+extern "C" MXFP8_API int mxfp8_dequantize(const void* q, int64_t rows, int64_t cols, int64_t ld_q, const void* s, void* out,
+                                int out_dtype, int64_t ld_out, mxfp8_stream_t stream) {
+    if (out_dtype != MXFP8_BF16 && out_dtype != MXFP8_FP16 && out_dtype != MXFP8_F32) return MXFP8_ERR_DTYPE;
+    if (rows < 0 || cols < 0 || cols % 32 != 0 || ld_q < cols || ld_out < cols) return MXFP8_ERR_SHAPE;
+    if (rows == 0 || cols == 0) return MXFP8_OK;
+    if (!q || !s || !out) return MXFP8_ERR_NULL_POINTER;
+    if (!aligned(out, out_dtype == MXFP8_F32 ? 4 : 2)) return MXFP8_ERR_ALIGNMENT;
+    DeviceState* dev = nullptr;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    return launch_dequantize(static_cast<const uint8_t*>(q), rows, cols, ld_q, static_cast<const uint8_t*>(s), out,
+                             out_dtype, ld_out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" MXFP8_API int mxfp8_device_status(uint32_t* status_out, int clear) {
+    if (!status_out) return MXFP8_ERR_NULL_POINTER;
+    DeviceState* dev = nullptr;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    *status_out = 0;
+    if (!dev->status) return MXFP8_OK;
+    cudaError_t e = cudaMemcpy(status_out, dev->status, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(dev->status, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) {
+        set_last_error("mxfp8_device_status", (int)e);
+        return MXFP8_ERR_CUDA;
+    }
+    return MXFP8_OK;
+}
+
+extern "C" MXFP8_API const char* mxfp8_strerror(int status) {
+    switch (status) {
+        case MXFP8_OK: return "success";
+        case MXFP8_ERR_NULL_POINTER: return "a required pointer is NULL";
+        case MXFP8_ERR_SHAPE: return "sizes out of range or inconsistent";
+        case MXFP8_ERR_DTYPE: return "unsupported dtype";
+        case MXFP8_ERR_ALIGNMENT: return "a pointer or stride breaks the alignment contract";
+        case MXFP8_ERR_SCALE_BUFFER: return "the scale buffer is smaller than required";
+        case MXFP8_ERR_CUDA: return "a CUDA runtime call failed";
+        case MXFP8_ERR_TENSOR_MAP: return "the driver rejected a TMA descriptor";
+        case MXFP8_ERR_DEVICE: return "no usable sm_100 device is current";
+        default: return "unknown status";
+    }
+}
+
+extern "C" MXFP8_API const char* mxfp8_last_error(void) { return g_last_error.c_str(); }

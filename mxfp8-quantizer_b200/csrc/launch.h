@@ -1,0 +1,32 @@
+// launch.h -- internal host-side launch interface between the C ABI
+// (capi.cu) and the kernel translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mxfp8 {
+
+// Problem description after argument validation.
+struct QuantizeArgs {
+    const void* x;
+    int dtype;
+    int64_t m, k, ld_x;
+    uint8_t* q;
+    int64_t q_rows, q_cols, ld_q;
+    uint8_t* s;
+    int64_t scale_rows;   // q_rows rounded up to 128
+    int64_t scale_cols;   // q_cols / 32
+    int64_t col_chunks;   // ceil(scale_cols / 4)
+    unsigned int* status; // device error word (may be null)
+};
+
+// Returned by launchers: 0, or a negative mxfp8_status.
+int launch_quantize_tma(const QuantizeArgs& a, int sm_count, cudaStream_t stream);
+int launch_quantize_generic(const QuantizeArgs& a, int sm_count, cudaStream_t stream);
+int launch_dequantize(const uint8_t* q, int64_t rows, int64_t cols, int64_t ld_q, const uint8_t* s,
+                      void* out, int out_dtype, int64_t ld_out, cudaStream_t stream);
+
+// Records the CUDA error text for mxfp8_last_error() on this host thread.
+void set_last_error(const char* what, int code);
+
+}  // namespace mxfp8

@@ -1,0 +1,638 @@
+"""Host side of the B200 MXFP8 quantizer, mirroring the reference's Python API.
+
+Same public names, argument meanings, return-dict keys and exception types
+as the reference module (MXFP8_quantizer.py), backed by libmxfp8.so:
+
+- ``run_quantizer``            MXFP8_quantizer.py:863-1035 / 1304-1329
+- ``prepare_and_quantize``     MXFP8_quantizer.py:809-861 / 1362-1366
+- ``run_e2e_verification``     MXFP8_quantizer.py:1037-1223 / 1331-1350
+- ``run_e2e_suite``            MXFP8_quantizer.py:1225-1289 / 1352-1360
+- ``shape_problem``, ``packed_scale_storage_bytes``, ``packed_scale_word_count``,
+  ``materialize_quantizer_buffers``, ``verify_quantizer_outputs``,
+  ``reference_quantize``, ``decode_scale_bytes``, ``check_cuda_launch_errors``
+
+Differences that a caller can see:
+
+- No host pad copy.  The kernel reads X in place (any row stride) and
+  zero-fills outside (m, k) on the fly, so ``buffers["x"]`` is the caller's
+  unpadded tensor; Q and S still have the reference's padded launch shape
+  and identical bytes (scale 127 in padded columns, 0 in rows past the
+  launch shape).
+- Q and S are allocated uninitialised: the kernel writes every byte.
+- The end-to-end consumer is cuBLASLt's block-scaled GEMM (through
+  ``torch._scaled_mm`` with e8m0 scales in the same 128x4 chunk layout)
+  instead of the vendored CuTeDSL GEMM; ``mma_tiler_mn`` and
+  ``cluster_shape_mn`` are validated with the reference's rules and
+  reported, but the library picks its own tiling.
+- The verifier follows the kernel on inf/NaN blocks (the reference's torch
+  restatement gives scale 256 there), and our payload is bit-exact
+  (``q_max_byte_diff`` 0); the pass rule keeps the reference's 2-ULP bound.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import statistics
+from typing import Any
+
+import torch
+
+from . import _capi
+
+FP8_E4M3_MAX = 448.0
+Q_BYTE_DIFF_TOLERANCE = 2
+SCALE_VEC_SIZE = 32
+SCALE_PACK_COLS = 4
+SCALE_ROWS_PER_PACK = 128
+DEFAULT_ROWS_PER_CTA = 8
+DEFAULT_K_TILE = 256
+_GRID_DIM_Y_LIMIT = 65535
+_INT32_MAX = 2 ** 31 - 1
+
+# (m, n, k, dtype, seed, mma_tiler_mn, cluster_shape_mn): the reference's
+# end-to-end suite (MXFP8_quantizer.py:23-38), kept so suite runs compare.
+DEFAULT_E2E_SUITE: tuple[tuple[int, int, int, str, int, tuple[int, int], tuple[int, int]], ...] = (
+    (1024, 1024, 2048, "bf16", 0, (128, 128), (1, 1)),
+    (2048, 2048, 2048, "bf16", 1, (128, 128), (2, 1)),
+    (1024, 2048, 4096, "fp16", 2, (128, 128), (1, 2)),
+    (2048, 2048, 4096, "bf16", 0, (256, 128), (2, 1)),
+    (2048, 1024, 2048, "fp16", 1, (256, 128), (2, 2)),
+    (1024, 1024, 2048, "bf16", 3, (128, 64), (1, 1)),
+)
+
+
+@dataclasses.dataclass(frozen=True)
+class MXFP8QuantizerConfig:
+    """Launch configuration accepted for compatibility (MXFP8_quantizer.py:235-260).
+
+    The B200 kernel picks its own tiling (128x128 tiles, persistent CTAs);
+    ``rows_per_cta`` and ``k_tile`` only define the reference's padded
+    launch shape and are validated with the reference's rules."""
+
+    input_dtype: torch.dtype = torch.bfloat16
+    rows_per_cta: int = DEFAULT_ROWS_PER_CTA
+    k_tile: int = DEFAULT_K_TILE
+
+    threads_per_cta = 288  # 8 compute warps + 1 TMA producer warp
+
+    @property
+    def blocks_per_tile(self) -> int:
+        return self.k_tile // SCALE_VEC_SIZE
+
+    def validate(self) -> None:
+        if self.k_tile % SCALE_VEC_SIZE != 0:
+            raise ValueError("k_tile must be divisible by 32")
+        if self.rows_per_cta != 8:
+            raise ValueError("the launch shape requires rows_per_cta=8")
+        if self.blocks_per_tile % SCALE_PACK_COLS != 0:
+            raise ValueError("blocks_per_tile must be divisible by 4")
+        if self.input_dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("the quantizer only supports bf16/fp16 inputs")
+
+
+def ceil_div(a: int, b: int) -> int:
+    return (a + b - 1) // b
+
+
+def packed_scale_storage_bytes(m: int, k: int, scale_vec_size: int = SCALE_VEC_SIZE) -> int:
+    scale_cols = ceil_div(k, scale_vec_size)
+    return ceil_div(m, SCALE_ROWS_PER_PACK) * SCALE_ROWS_PER_PACK * ceil_div(scale_cols, SCALE_PACK_COLS) * SCALE_PACK_COLS
+
+
+def packed_scale_word_count(m: int, k: int, scale_vec_size: int = SCALE_VEC_SIZE) -> int:
+    return packed_scale_storage_bytes(m, k, scale_vec_size) // 4
+
+
+def shape_problem(m: int, k: int, rows_per_cta: int = DEFAULT_ROWS_PER_CTA, k_tile: int = DEFAULT_K_TILE):
+    """Logical (m, k) -> the reference's padded launch shape, same limits and
+    messages as MXFP8_quantizer.py:766-791."""
+    if m < 1 or k < 1:
+        raise ValueError(f"m and k must be >= 1, got m={m}, k={k}")
+    if m > _INT32_MAX or k > _INT32_MAX:
+        raise ValueError(
+            f"m and k must fit Int32 (<= {_INT32_MAX}) because they are passed "
+            f"to the kernel as Int32 scalars, got m={m}, k={k}")
+    kernel_m = ceil_div(m, rows_per_cta) * rows_per_cta
+    kernel_k = ceil_div(k, k_tile) * k_tile
+    grid_m = kernel_m // rows_per_cta
+    grid_k = kernel_k // k_tile
+    if grid_m > _INT32_MAX:
+        raise ValueError(f"gridDim.x limit exceeded: {grid_m} row-tiles > {_INT32_MAX}")
+    if grid_k > _GRID_DIM_Y_LIMIT:
+        raise ValueError(
+            f"gridDim.y limit exceeded: k={k} with k_tile={k_tile} needs "
+            f"grid_k={grid_k} > {_GRID_DIM_Y_LIMIT} K-tiles. Reduce k_tile or reshape the problem.")
+    return kernel_m, kernel_k, grid_m, grid_k
+
+
+def _resolve_input_dtype(dtype_name: str) -> torch.dtype:
+    name = dtype_name.lower()
+    if name == "bf16":
+        return torch.bfloat16
+    if name == "fp16":
+        return torch.float16
+    raise ValueError("input_dtype must be one of: bf16, fp16")
+
+
+def _dtype_code(t: torch.dtype) -> int:
+    if t == torch.bfloat16:
+        return _capi.BF16
+    if t == torch.float16:
+        return _capi.FP16
+    raise ValueError("input_dtype must be one of: bf16, fp16")
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _check_buffer_alignment(name: str, tensor: torch.Tensor, required_bytes: int) -> None:
+    if tensor.data_ptr() % required_bytes != 0:
+        raise ValueError(
+            f"{name} buffer must be {required_bytes}-byte aligned, got data_ptr={tensor.data_ptr()} "
+            f"(misaligned by {tensor.data_ptr() % required_bytes} bytes)")
+
+
+def _as_row_major(x: torch.Tensor) -> torch.Tensor:
+    if x.dim() != 2:
+        raise ValueError(f"X must be 2-D, got shape {tuple(x.shape)}")
+    if x.stride(1) != 1 or x.stride(0) < x.shape[1]:
+        x = x.contiguous()
+    return x
+
+
+def quantize(x: torch.Tensor, q: torch.Tensor | None = None, s: torch.Tensor | None = None,
+             q_rows: int | None = None, q_cols: int | None = None, stream=None):
+    """Quantize a CUDA (m, k) bf16/fp16 tensor; returns (q e4m3 (q_rows, q_cols), s uint8 packed).
+
+    ``q_rows``/``q_cols`` default to the reference's padded launch shape.
+    Pass ``q_rows=m, q_cols=ceil(k/32)*32`` for the tight layout (padding
+    scale bytes 0).  Preallocated ``q``/``s`` are written in place."""
+    x = _as_row_major(x)
+    m, k = x.shape
+    if q_rows is None or q_cols is None:
+        km, kk, _, _ = shape_problem(max(m, 1), max(k, 1))
+        q_rows = km if q_rows is None else q_rows
+        q_cols = kk if q_cols is None else q_cols
+    if q is None:
+        q = torch.empty((q_rows, q_cols), dtype=torch.float8_e4m3fn, device=x.device)
+    if s is None:
+        s = torch.empty((_capi.scale_storage_bytes(q_rows, q_cols),), dtype=torch.uint8, device=x.device)
+    if q.dim() != 2 or q.shape[0] < q_rows or q.stride(1) != 1:
+        raise ValueError("q must be a row-major (q_rows, >= q_cols) byte matrix")
+    with torch.cuda.device(x.device):
+        _capi.quantize(x.data_ptr(), _dtype_code(x.dtype), m, k, x.stride(0), q.data_ptr(), q_rows, q_cols,
+                       q.stride(0), s.data_ptr(), s.numel() * s.element_size(), _stream_handle(stream))
+    return q, s
+
+
+def dequantize(q: torch.Tensor, s: torch.Tensor, out_dtype: torch.dtype = torch.float32, stream=None):
+    """E4M3 payload + packed UE8M0 scales -> out_dtype (bf16, fp16 or fp32)."""
+    rows, cols = q.shape
+    code = {torch.float32: _capi.F32, torch.bfloat16: _capi.BF16, torch.float16: _capi.FP16}[out_dtype]
+    out = torch.empty((rows, cols), dtype=out_dtype, device=q.device)
+    with torch.cuda.device(q.device):
+        _capi.dequantize(q.data_ptr(), rows, cols, q.stride(0), s.data_ptr(), out.data_ptr(), code, out.stride(0),
+                         _stream_handle(stream))
+    return out
+
+
+class HostQuantizer:
+    """Quantize a host-resident (m, k) matrix into host-resident Q and S.
+
+    Rows move in chunks of ``chunk_rows`` (a multiple of 128, so every
+    chunk's scales are one contiguous slice of S) through three streams:
+    host->device copy, kernel, device->host copy of Q and S, so both copy
+    directions and the kernel overlap.  Device staging buffers are allocated
+    once here.  Pass pinned host tensors; pageable ones still work but do
+    not overlap.  The output geometry is the tight one, (m, ceil(k/32)*32)."""
+
+    def __init__(self, m: int, k: int, dtype: torch.dtype = torch.bfloat16, device=None, chunk_rows: int = 1024):
+        if chunk_rows % SCALE_ROWS_PER_PACK or chunk_rows <= 0:
+            raise ValueError("chunk_rows must be a positive multiple of 128")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.m, self.k, self.dtype = m, k, dtype
+        self.q_cols = ceil_div(k, SCALE_VEC_SIZE) * SCALE_VEC_SIZE
+        self.s_bytes = _capi.scale_storage_bytes(m, self.q_cols)
+        self.chunk_rows = chunk_rows
+        self.x = torch.empty((m, k), dtype=dtype, device=self.device)
+        self.q = torch.empty((m, self.q_cols), dtype=torch.uint8, device=self.device)
+        self.s = torch.empty((self.s_bytes,), dtype=torch.uint8, device=self.device)
+        self.streams = [torch.cuda.Stream(self.device) for _ in range(3)]
+        self.chunks = [(r0, min(m, r0 + chunk_rows)) for r0 in range(0, m, chunk_rows)]
+        self.launches_per_call = len(self.chunks)
+
+    def __call__(self, x_host: torch.Tensor, q_host: torch.Tensor, s_host: torch.Tensor) -> None:
+        h2d, comp, d2h = self.streams
+        cur = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(cur)
+        for st in self.streams:
+            st.wait_event(start)
+        per_chunk_s = _capi.scale_storage_bytes(self.chunk_rows, self.q_cols)
+        code = _dtype_code(self.dtype)
+        for r0, r1 in self.chunks:
+            rows = r1 - r0
+            s0 = (r0 // self.chunk_rows) * per_chunk_s
+            s_len = _capi.scale_storage_bytes(rows, self.q_cols)
+            with torch.cuda.stream(h2d):
+                self.x[r0:r1].copy_(x_host[r0:r1], non_blocking=True)
+                loaded = torch.cuda.Event()
+                loaded.record(h2d)
+            comp.wait_event(loaded)
+            _capi.quantize(self.x[r0].data_ptr(), code, rows, self.k, self.k, self.q[r0].data_ptr(), rows,
+                           self.q_cols, self.q_cols, self.s.data_ptr() + s0, s_len, comp.cuda_stream)
+            done = torch.cuda.Event()
+            done.record(comp)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                q_host[r0:r1].copy_(self.q[r0:r1], non_blocking=True)
+                s_host[s0:s0 + s_len].copy_(self.s[s0:s0 + s_len], non_blocking=True)
+        end = torch.cuda.Event()
+        end.record(d2h)
+        cur.wait_event(end)
+
+
+class CompiledQuantizer:
+    """Stand-in for the reference's compiled callable (MXFP8_quantizer.py:699-728).
+
+    Called as ``(x_ptr, q_dwords_ptr, s_words_ptr, kernel_m, kernel_k,
+    s_word_count, stream)`` like the CuTeDSL callable; it remembers the
+    logical (m, k) and row stride of X, because X is read unpadded."""
+
+    def __init__(self, dtype: torch.dtype, m: int, k: int, ld_x: int | None = None):
+        self.dtype_code = _dtype_code(dtype)
+        self.m, self.k = m, k
+        self.ld_x = k if ld_x is None else ld_x
+
+    def __call__(self, x_ptr, q_dwords_ptr, s_words_ptr, m, k, s_word_count, stream=None) -> None:
+        kernel_m, kernel_k = int(m), int(k)
+        _capi.quantize(int(x_ptr), self.dtype_code, self.m, self.k, self.ld_x, int(q_dwords_ptr), kernel_m,
+                       kernel_k, kernel_k, int(s_words_ptr), int(s_word_count) * 4, _stream_handle(stream))
+
+
+def materialize_quantizer_buffers(m: int, k: int, torch_input_dtype: torch.dtype, x_source: torch.Tensor):
+    """Output buffers for the padded launch shape (m, k) = (kernel_m, kernel_k).
+
+    Same keys as MXFP8_quantizer.py:554-608.  X is not copied: ``x`` is the
+    caller's tensor (row-major, any row stride); Q and S are left
+    uninitialised because the kernel writes every byte."""
+    if x_source.dtype != torch_input_dtype:
+        raise ValueError(f"x dtype {x_source.dtype} does not match {torch_input_dtype}")
+    x = _as_row_major(x_source)
+    if x.shape[0] > m or x.shape[1] > k:
+        raise ValueError(f"x of shape {tuple(x.shape)} does not fit the launch shape ({m}, {k})")
+    q = torch.empty((m, k), dtype=torch.float8_e4m3fn, device=x.device)
+    word_count = packed_scale_word_count(m, k)
+    s_words = torch.empty((word_count,), dtype=torch.uint32, device=x.device)
+    _check_buffer_alignment("x", x, 2)
+    _check_buffer_alignment("q", q, 8)
+    _check_buffer_alignment("s", s_words, 4)
+    return {
+        "x": x,
+        "q_fp8": q,
+        "q_bytes": q.view(torch.int8),
+        "s_storage_bytes": s_words.view(torch.uint8),
+        "s_storage_word_count": word_count,
+        "x_ptr": x.data_ptr(),
+        "q_dwords_ptr": q.data_ptr(),
+        "s_words_ptr": s_words.data_ptr(),
+    }
+
+
+def check_cuda_launch_errors(stream=None, context: str = "kernel launch") -> None:
+    """Synchronise the stream and surface device errors, including the
+    library's sticky device status word (bounded pipeline waits)."""
+    try:
+        if stream is None:
+            torch.cuda.current_stream().synchronize()
+        elif isinstance(stream, torch.cuda.Stream):
+            stream.synchronize()
+        else:
+            torch.cuda.ExternalStream(int(stream)).synchronize()
+    except RuntimeError as exc:  # surfaced by the CUDA runtime
+        raise RuntimeError(f"CUDA error after {context}: {exc}") from exc
+    status = _capi.device_status(clear=True)
+    if status:
+        raise RuntimeError(f"CUDA error after {context}: device status word {status:#x} (pipeline wait timed out)")
+
+
+# --------------------------------------------------------------------------
+# verifier (torch; follows the kernel, including inf/NaN blocks)
+# --------------------------------------------------------------------------
+
+def _bits_to_f32(bits_i32: torch.Tensor) -> torch.Tensor:
+    return bits_i32.to(torch.int32).view(torch.float32)
+
+
+def reference_quantize(x_padded: torch.Tensor):
+    """Torch restatement of the recipe (MXFP8_quantizer.py:610-641) with the
+    kernel's handling of inf/NaN blocks (MXFP8_quantizer.py:170-200, 473-501).
+    Returns (scale bytes int32 (m, k/32), q fp8 (m, k))."""
+    m, k = x_padded.shape
+    bits = x_padded.contiguous().view(torch.int16).to(torch.int32) & 0x7FFF
+    amax_bits = bits.view(m, k // SCALE_VEC_SIZE, SCALE_VEC_SIZE).amax(dim=2)
+    if x_padded.dtype == torch.bfloat16:
+        amax = _bits_to_f32(amax_bits << 16)
+    else:
+        amax = amax_bits.to(torch.int16).view(torch.float16).to(torch.float32)
+    # fma.rn(amax, f32(1/448), f32(1e-12)) == round_f32(amax * c + eps in fp64) for every 16-bit amax
+    c = torch.tensor(1.0 / FP8_E4M3_MAX, dtype=torch.float32).double().item()
+    eps = torch.tensor(1.0e-12, dtype=torch.float32).double().item()
+    scaled = (amax.to(torch.float64) * c + eps).to(torch.float32)
+    sb = scaled.view(torch.int32)
+    e = ((sb >> 23) & 0xFF) + ((sb & 0x7FFFFF) != 0).to(torch.int32)
+    e = torch.where(amax_bits == 0, torch.full_like(e, 127), e)
+    scale_bytes = e & 0xFF
+    inv_bits = ((254 - e.to(torch.int64)) << 23) & 0xFFFFFFFF
+    inv_bits = torch.where(inv_bits >= 2 ** 31, inv_bits - 2 ** 32, inv_bits)
+    inv = _bits_to_f32(inv_bits)
+    prod = x_padded.to(torch.float32) * inv.repeat_interleave(SCALE_VEC_SIZE, dim=1)
+    q = prod.clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
+    qb = torch.where(torch.isnan(prod), torch.full_like(prod, 0x7F, dtype=torch.uint8), q.view(torch.uint8))
+    return scale_bytes, qb.view(torch.float8_e4m3fn)
+
+
+def decode_scale_bytes(s_bytes: torch.Tensor, m: int, k: int) -> torch.Tensor:
+    """Packed chunk layout -> dense (m, ceil(k/32)) scale bytes
+    (the layout map of MXFP8_quantizer.py:643-662)."""
+    scale_cols = ceil_div(k, SCALE_VEC_SIZE)
+    packed_col_blocks = ceil_div(scale_cols, SCALE_PACK_COLS)
+    rows = torch.arange(m, device=s_bytes.device)[:, None]
+    cols = torch.arange(scale_cols, device=s_bytes.device)[None, :]
+    rr = rows % SCALE_ROWS_PER_PACK
+    offs = ((rows // SCALE_ROWS_PER_PACK) * packed_col_blocks + cols // SCALE_PACK_COLS) * 512 \
+        + (rr % 32) * 16 + (rr // 32) * 4 + cols % SCALE_PACK_COLS
+    return s_bytes[offs]
+
+
+def verify_quantizer_outputs(buffers, kernel_m: int, kernel_k: int, real_m: int, real_k: int):
+    """Compare Q/S with the torch restatement over the real region
+    (MXFP8_quantizer.py:664-697): S bit-exact, Q within Q_BYTE_DIFF_TOLERANCE."""
+    x = buffers["x"]
+    x_padded = torch.zeros((kernel_m, kernel_k), dtype=x.dtype, device=x.device)
+    x_padded[: x.shape[0], : x.shape[1]] = x
+    scale_ref, q_ref = reference_quantize(x_padded)
+    q_bytes = buffers["q_fp8"].view(torch.uint8).to(torch.int32)
+    q_diff = (q_bytes - q_ref.view(torch.uint8).to(torch.int32)).abs()[:real_m, :real_k]
+    q_max_byte_diff = int(q_diff.max().item())
+    q_exact_fraction = float((q_diff == 0).float().mean().item())
+    dense = decode_scale_bytes(buffers["s_storage_bytes"], kernel_m, kernel_k)
+    real_cols = ceil_div(real_k, SCALE_VEC_SIZE)
+    scale_bytes_exact = bool((dense[:real_m, :real_cols].to(torch.int32) == scale_ref[:real_m, :real_cols]).all().item())
+    return {
+        "verification_passed": scale_bytes_exact and q_max_byte_diff <= Q_BYTE_DIFF_TOLERANCE,
+        "q_max_byte_diff": q_max_byte_diff,
+        "q_exact_fraction": q_exact_fraction,
+        "scale_bytes_exact": scale_bytes_exact,
+    }
+
+
+# --------------------------------------------------------------------------
+# entry points
+# --------------------------------------------------------------------------
+
+def prepare_and_quantize(m: int, k: int, dtype_name: str, seed: int, stream=None) -> dict[str, Any]:
+    """Quantize one seeded (m, k) matrix end to end: shape, launch, verify
+    (MXFP8_quantizer.py:809-861)."""
+    torch.manual_seed(seed)
+    torch_dtype = _resolve_input_dtype(dtype_name)
+    kernel_m, kernel_k, _, _ = shape_problem(m, k, DEFAULT_ROWS_PER_CTA, DEFAULT_K_TILE)
+    x = torch.randn((m, k), dtype=torch_dtype, device="cuda")
+    buffers = materialize_quantizer_buffers(kernel_m, kernel_k, torch_dtype, x)
+    compiled = CompiledQuantizer(torch_dtype, m, k, buffers["x"].stride(0))
+    compiled(buffers["x_ptr"], buffers["q_dwords_ptr"], buffers["s_words_ptr"], kernel_m, kernel_k,
+             buffers["s_storage_word_count"], stream)
+    torch.cuda.synchronize()
+    check_cuda_launch_errors(stream, "quantizer launch")
+    verify = verify_quantizer_outputs(buffers, kernel_m, kernel_k, m, k)
+    if not verify["verification_passed"]:
+        raise ValueError(f"quantizer verification failed for ({m}, {k}): {verify}")
+    return {"m": m, "k": k, "kernel_m": kernel_m, "kernel_k": kernel_k, "x": x, "buffers": buffers,
+            "compiled": compiled, "verify": verify}
+
+
+def _l2_bytes() -> int:
+    return int(torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size)
+
+
+def benchmark_compiled_quantizer(launch, stream: int, warmup: int, iters: int, workspaces: list, repeats: int):
+    """min/mean/std over `repeats` passes of: `warmup` launches, then CUDA
+    events around `iters` launches, mean per launch (the timing rule of
+    MXFP8_quantizer.py:730-761 and the CuTeDSL testing.benchmark it calls)."""
+    samples_us = []
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    ext = torch.cuda.ExternalStream(stream)
+    n = len(workspaces)
+    for _ in range(repeats):
+        idx = 0
+        for _ in range(warmup):
+            launch(*workspaces[idx])
+            idx = (idx + 1) % n
+        start.record(ext)
+        for _ in range(iters):
+            launch(*workspaces[idx])
+            idx = (idx + 1) % n
+        end.record(ext)
+        end.synchronize()
+        samples_us.append(start.elapsed_time(end) * 1000.0 / max(iters, 1))
+    mn, mean = min(samples_us), statistics.fmean(samples_us)
+    std = statistics.pstdev(samples_us) if len(samples_us) > 1 else 0.0
+    return {"min_runtime_us": mn, "mean_runtime_us": mean, "std_runtime_us": std,
+            "min_runtime_s": mn * 1e-6, "mean_runtime_s": mean * 1e-6, "std_runtime_s": std * 1e-6}
+
+
+def run_quantizer(m: int = 16384, k: int = 16384, rows_per_cta: int = DEFAULT_ROWS_PER_CTA,
+                  k_tile: int = DEFAULT_K_TILE, input_dtype: str = "bf16", warmup_iterations: int = 10,
+                  iterations: int = 50, benchmark_repeats: int = 5, cold_l2: bool = False,
+                  skip_verification: bool = False, seed: int = 0) -> dict[str, Any]:
+    """Quantize + verify + benchmark one (m, k) problem (MXFP8_quantizer.py:863-1035)."""
+    torch.manual_seed(seed)
+    dtype_name = input_dtype.lower()
+    torch_dtype = _resolve_input_dtype(input_dtype)
+    cfg = MXFP8QuantizerConfig(torch_dtype, rows_per_cta, k_tile)
+    cfg.validate()
+    x = torch.randn((m, k), dtype=torch_dtype, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    is_full_tile = (m % rows_per_cta == 0) and (k % k_tile == 0)
+    kernel_m, kernel_k, grid_m, grid_k = shape_problem(m, k, rows_per_cta, k_tile)
+    buffers = materialize_quantizer_buffers(kernel_m, kernel_k, torch_dtype, x)
+    compiled = CompiledQuantizer(torch_dtype, m, k, buffers["x"].stride(0))
+
+    def args_of(b):
+        return (b["x_ptr"], b["q_dwords_ptr"], b["s_words_ptr"], kernel_m, kernel_k, b["s_storage_word_count"],
+                stream)
+
+    verify_results = None
+    if not skip_verification:
+        compiled(*args_of(buffers))
+        torch.cuda.synchronize()
+        check_cuda_launch_errors(stream, "quantizer verification launch")
+        verify_results = verify_quantizer_outputs(buffers, kernel_m, kernel_k, m, k)
+        if not verify_results["verification_passed"]:
+            raise ValueError(
+                "MXFP8 quantizer correctness check FAILED: "
+                f"scale bytes bit-exact={verify_results['scale_bytes_exact']}, "
+                f"fp8 payload max byte diff={verify_results['q_max_byte_diff']} "
+                f"(tolerance {Q_BYTE_DIFF_TOLERANCE}), "
+                f"exact byte fraction={verify_results['q_exact_fraction']:.6f}")
+        print("Correctness check passed: "
+              f"scale bytes bit-exact={verify_results['scale_bytes_exact']}, "
+              f"fp8 payload max byte diff={verify_results['q_max_byte_diff']}, "
+              f"exact byte fraction={verify_results['q_exact_fraction']:.6f}")
+
+    logical_bytes_moved = 2 * m * k + m * k + m * (k // SCALE_VEC_SIZE)
+    physical_bytes_moved = 2 * kernel_m * kernel_k + kernel_m * kernel_k + kernel_m * (kernel_k // SCALE_VEC_SIZE)
+    one_workspace_bytes = (x.numel() * x.element_size() + buffers["q_bytes"].numel()
+                           + buffers["s_storage_bytes"].numel())
+    workspace_count = 1
+    if cold_l2:
+        workspace_count = min(warmup_iterations + iterations, (_l2_bytes() * 3) // one_workspace_bytes + 1)
+    workspaces = [args_of(buffers)]
+    keep = [buffers]
+    for _ in range(workspace_count - 1):
+        wx = torch.randn((m, k), dtype=torch_dtype, device="cuda")
+        wb = materialize_quantizer_buffers(kernel_m, kernel_k, torch_dtype, wx)
+        keep.append(wb)
+        workspaces.append(args_of(wb))
+    if workspace_count > 1:  # flush L2 after creating the workspaces
+        flush = torch.empty(_l2_bytes() * 2 // 4, dtype=torch.int32, device="cuda")
+        flush.zero_()
+        del flush
+    timing = benchmark_compiled_quantizer(compiled, stream, warmup_iterations, iterations, workspaces,
+                                          benchmark_repeats)
+    check_cuda_launch_errors(stream, "quantizer benchmark")
+    rmin, rmean, rstd = timing["min_runtime_s"], timing["mean_runtime_s"], timing["std_runtime_s"]
+    v = verify_results
+    return {
+        "launch_success": True,
+        "verification_ran": v is not None,
+        "verification_passed": v["verification_passed"] if v is not None else None,
+        "q_max_byte_diff": v["q_max_byte_diff"] if v is not None else None,
+        "q_exact_fraction": v["q_exact_fraction"] if v is not None else None,
+        "scale_bytes_exact": v["scale_bytes_exact"] if v is not None else None,
+        "input_dtype": dtype_name,
+        "rows_per_cta": cfg.rows_per_cta,
+        "k_tile": cfg.k_tile,
+        "threads_per_cta": cfg.threads_per_cta,
+        "blocks_per_tile": cfg.blocks_per_tile,
+        "kernel_m": kernel_m,
+        "kernel_k": kernel_k,
+        "grid_m": grid_m,
+        "grid_k": grid_k,
+        "total_ctas": grid_m * grid_k,
+        "runtime_min_s": rmin,
+        "runtime_mean_s": rmean,
+        "runtime_std_s": rstd,
+        "runtime_min_us": timing["min_runtime_us"],
+        "runtime_mean_us": timing["mean_runtime_us"],
+        "runtime_std_us": timing["std_runtime_us"],
+        "effective_gb_s": logical_bytes_moved / rmin / 1.0e9,
+        "effective_gb_s_mean": logical_bytes_moved / rmean / 1.0e9,
+        "effective_tb_s": logical_bytes_moved / rmin / 1.0e12,
+        "logical_bytes_moved": logical_bytes_moved,
+        "physical_bytes_moved": physical_bytes_moved,
+        "benchmark_repeats": benchmark_repeats,
+        "workspace_count": workspace_count,
+        "cold_l2": cold_l2,
+        "is_full_tile": is_full_tile,
+        "dispatch_mode": "b200_tma_full_tile" if is_full_tile else "b200_tma_ragged",
+    }
+
+
+def blockscaled_gemm(a_q: torch.Tensor, b_q: torch.Tensor, a_s: torch.Tensor, b_s: torch.Tensor) -> torch.Tensor:
+    """C (m, n) fp32 = (A * SFA) @ (B * SFB)^T on the tcgen05 block-scaled path
+    (cuBLASLt via torch._scaled_mm), reading the packed scales unmodified."""
+    return torch._scaled_mm(a_q, b_q.t(), scale_a=a_s.view(torch.float8_e8m0fnu),
+                            scale_b=b_s.view(torch.float8_e8m0fnu), out_dtype=torch.float32)
+
+
+def run_e2e_verification(m: int = 1024, n: int = 1024, k: int = 2048, input_dtype: str = "bf16", seed: int = 0,
+                         gemm_tolerance: float = 1.0e-2, mma_tiler_mn: tuple[int, int] = (128, 128),
+                         cluster_shape_mn: tuple[int, int] = (1, 1)) -> dict[str, Any]:
+    """Quantize A (m, k) and B (n, k) and feed Q/S unmodified into a
+    block-scaled GEMM; compare with fp32 (MXFP8_quantizer.py:1037-1223)."""
+    if mma_tiler_mn[0] not in (128, 256) or mma_tiler_mn[1] not in (64, 128, 192, 256):
+        raise ValueError(f"mma_tiler_mn must be M in (128, 256) and N in (64, 128, 192, 256), got {mma_tiler_mn}")
+
+    def pow2(v):
+        return v > 0 and (v & (v - 1)) == 0
+
+    if (not pow2(cluster_shape_mn[0]) or not pow2(cluster_shape_mn[1]) or cluster_shape_mn[0] > 4
+            or cluster_shape_mn[1] > 4 or cluster_shape_mn[0] * cluster_shape_mn[1] > 16):
+        raise ValueError(f"cluster_shape_mn entries must be powers of two in [1, 4] with a product <= 16, "
+                         f"got {cluster_shape_mn}")
+    if mma_tiler_mn[0] == 256 and cluster_shape_mn[0] % 2 != 0:
+        raise ValueError(f"cluster_shape_mn[0] must be a multiple of 2 when mma_tiler_mn[0] == 256, "
+                         f"got cluster_shape_mn={cluster_shape_mn}")
+    if m % mma_tiler_mn[0] != 0 or n % mma_tiler_mn[1] != 0:
+        raise ValueError(f"GEMM consumer requires M % {mma_tiler_mn[0]} == 0 and N % {mma_tiler_mn[1]} == 0 "
+                         f"for mma_tiler_mn={mma_tiler_mn}, got m={m}, n={n}")
+    if k % DEFAULT_K_TILE != 0:
+        raise ValueError(f"GEMM consumer requires K % {DEFAULT_K_TILE} == 0, got k={k}")
+    torch.manual_seed(seed)
+    stream = torch.cuda.current_stream().cuda_stream
+    a_res = prepare_and_quantize(m, k, input_dtype, seed, stream)
+    b_res = prepare_and_quantize(n, k, input_dtype, seed + 1, stream)
+    a_q, b_q = a_res["buffers"]["q_fp8"], b_res["buffers"]["q_fp8"]
+    a_s, b_s = a_res["buffers"]["s_storage_bytes"], b_res["buffers"]["s_storage_bytes"]
+    c = blockscaled_gemm(a_q, b_q, a_s, b_s)
+    torch.cuda.synchronize()
+    sfa = torch.exp2(decode_scale_bytes(a_s, m, k).to(torch.float32) - 127.0).repeat_interleave(SCALE_VEC_SIZE, 1)[:, :k]
+    sfb = torch.exp2(decode_scale_bytes(b_s, n, k).to(torch.float32) - 127.0).repeat_interleave(SCALE_VEC_SIZE, 1)[:, :k]
+    ref = (a_q.to(torch.float32) * sfa) @ (b_q.to(torch.float32) * sfb).T
+    abs_err = (c - ref).abs()
+    max_abs_err = float(abs_err.max().item())
+    max_err_ratio = float((abs_err / (gemm_tolerance + gemm_tolerance * ref.abs())).max().item())
+    pass_margin = 1.0 / max_err_ratio if max_err_ratio > 0 else float("inf")
+    torch.testing.assert_close(c, ref, rtol=gemm_tolerance, atol=gemm_tolerance)
+    print("End-to-end blockscaled GEMM check passed: "
+          f"max_abs_err={max_abs_err:.3e}, max_err_ratio={max_err_ratio:.3f} "
+          f"(atol=rtol={gemm_tolerance:.0e}, pass margin={pass_margin:.1f}x)")
+    return {
+        "e2e_verification_passed": True,
+        "m": m, "n": n, "k": k, "input_dtype": input_dtype,
+        "gemm_config": {"mma_tiler_mn": list(mma_tiler_mn), "cluster_shape_mn": list(cluster_shape_mn),
+                        "sf_vec_size": SCALE_VEC_SIZE, "sf_dtype": "Float8E8M0FNU", "a/b_dtype": "Float8E4M3FN",
+                        "c_dtype": "Float32", "consumer": "torch._scaled_mm (cuBLASLt block-scaled, 128x4 chunks)"},
+        "sfa_layout": "tcgen05_atom_layout_packed_direct",
+        "quantizer_verify_a": a_res["verify"],
+        "quantizer_verify_b": b_res["verify"],
+        "max_abs_err": max_abs_err,
+        "max_err_ratio": max_err_ratio,
+        "pass_margin": pass_margin,
+        "gemm_tolerance": gemm_tolerance,
+    }
+
+
+def run_e2e_suite(configs=DEFAULT_E2E_SUITE, gemm_tolerance: float = 1.0e-2) -> dict[str, Any]:
+    """Every config must pass (MXFP8_quantizer.py:1225-1289)."""
+    results = [run_e2e_verification(m=m, n=n, k=k, input_dtype=dt, seed=seed, gemm_tolerance=gemm_tolerance,
+                                    mma_tiler_mn=tiler, cluster_shape_mn=cluster)
+               for (m, n, k, dt, seed, tiler, cluster) in configs]
+    summary = []
+    for (m, n, k, dt, seed, tiler, cluster), r in zip(configs, results):
+        summary.append({"m": m, "n": n, "k": k, "input_dtype": dt, "seed": seed, "mma_tiler_mn": list(tiler),
+                        "cluster_shape_mn": list(cluster),
+                        "quantizer_verify_passed": r["quantizer_verify_a"]["verification_passed"]
+                        and r["quantizer_verify_b"]["verification_passed"],
+                        "max_abs_err": r["max_abs_err"], "max_err_ratio": r["max_err_ratio"],
+                        "pass_margin": r["pass_margin"]})
+    worst_abs = max(r["max_abs_err"] for r in results)
+    worst_ratio = max(r["max_err_ratio"] for r in results)
+    print(f"e2e suite passed: {len(results)}/{len(results)} configs "
+          f"(worst max_abs_err={worst_abs:.3e}, worst max_err_ratio={worst_ratio:.3f})")
+    return {"e2e_suite_passed": True, "num_configs": len(results), "gemm_tolerance": gemm_tolerance,
+            "configs": summary}
+
+
+def build_runtime() -> dict[str, Any]:
+    """Same keys as MXFP8_quantizer.build_runtime (MXFP8_quantizer.py:1291-1296)."""
+    _capi.lib()
+    return {"run_quantizer": run_quantizer, "run_e2e_verification": run_e2e_verification,
+            "run_e2e_suite": run_e2e_suite, "prepare_and_quantize": prepare_and_quantize}

@@ -1,0 +1,261 @@
+"""GPU parity: libmxfp8.so (called through its C ABI) against the CPU oracle
+and the reference-recipe digests.  Bit-exact on every byte of Q and of the
+packed scale storage."""
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+import inputs
+from make_golden import CASES
+
+pytestmark = pytest.mark.gpu
+
+RNG = np.random.default_rng(1234)
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@pytest.fixture(scope="module")
+def capi():
+    import MXFP8_quantizer
+
+    pkg = MXFP8_quantizer.load_package()
+    pkg._capi.lib()
+    assert torch.cuda.is_available()
+    return pkg._capi
+
+
+def to_dev(bits, pad_ld=None, offset_elems=0):
+    """bits (m, k) uint16 -> device tensor view with row stride pad_ld and a
+    start offset (for the strided / misaligned layouts)."""
+    m, k = bits.shape
+    ld = pad_ld or k
+    buf = torch.zeros(m * ld + offset_elems + 8, dtype=torch.int16, device="cuda")
+    view = buf[offset_elems:offset_elems + m * ld].view(m, ld)
+    view[:, :k] = torch.from_numpy(bits.view(np.int16)).cuda()
+    return buf, view, ld
+
+
+def gpu_quantize(capi, bits, dtype, q_rows, q_cols, ld_x=None, x_offset=0, q_offset=0, ld_q=None, garbage=0xAB,
+                 s_offset=0):
+    m, k = bits.shape
+    _, xv, ld = to_dev(bits, ld_x, x_offset)
+    ld_q = ld_q or q_cols
+    s_bytes = capi.scale_storage_bytes(q_rows, q_cols)
+    qbuf = torch.full((q_rows * ld_q + q_offset + 64,), garbage, dtype=torch.uint8, device="cuda")
+    sbuf = torch.full((s_bytes + s_offset + 64,), garbage, dtype=torch.uint8, device="cuda")
+    code = 0 if dtype == "bf16" else 1
+    capi.quantize(xv.data_ptr(), code, m, k, ld, qbuf.data_ptr() + q_offset, q_rows, q_cols, ld_q,
+                  sbuf.data_ptr() + s_offset, s_bytes, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert capi.device_status(clear=True) == 0
+    qb = qbuf.cpu().numpy()
+    sb = sbuf.cpu().numpy()
+    # bytes outside the output region must be untouched
+    assert (qb[:q_offset] == garbage).all() and (qb[q_offset + q_rows * ld_q:] == garbage).all()
+    assert (sb[:s_offset] == garbage).all() and (sb[s_offset + s_bytes:] == garbage).all()
+    q = qb[q_offset:q_offset + q_rows * ld_q].reshape(q_rows, ld_q)
+    if ld_q > q_cols:
+        assert (q[:, q_cols:] == garbage).all()
+    return np.ascontiguousarray(q[:, :q_cols]), sb[s_offset:s_offset + s_bytes]
+
+
+def check_against_oracle(capi, oracle_mod, bits, dtype, q_rows=None, q_cols=None, **kw):
+    m, k = bits.shape
+    if q_rows is None:
+        q_rows, q_cols = oracle_mod.padded_shape(max(m, 1), max(k, 1))
+    q_ref, s_ref = oracle_mod.quantize(bits, dtype, q_rows, q_cols)
+    q, s = gpu_quantize(capi, bits, dtype, q_rows, q_cols, **kw)
+    if not np.array_equal(q, q_ref):
+        bad = np.argwhere(q != q_ref)
+        r, c = bad[0]
+        raise AssertionError(f"payload mismatch at {len(bad)} bytes, first ({r},{c}): gpu {q[r, c]:#x} "
+                             f"oracle {q_ref[r, c]:#x}; x block = {bits[r, c // 32 * 32:(c // 32 + 1) * 32] if r < m else 'pad'}")
+    if not np.array_equal(s, s_ref):
+        bad = np.flatnonzero(s != s_ref)
+        raise AssertionError(f"scale mismatch at {len(bad)} bytes, first offset {bad[0]}: gpu {s[bad[0]]} "
+                             f"oracle {s_ref[bad[0]]}")
+    return q, s
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_reference_digests(name, capi, golden):
+    rec = golden["cases"][name]
+    desc, gen, dtype = CASES[name]
+    bits = gen()
+    q, s = gpu_quantize(capi, bits, dtype, rec["kernel_m"], rec["kernel_k"])
+    assert sha(q) == rec["q_sha256"], f"{name}: payload differs from the reference recipe"
+    assert sha(s) == rec["s_sha256"], f"{name}: packed scales differ from the reference recipe"
+
+
+@pytest.mark.parametrize("geometry", ["reference", "tight"])
+def test_special_values_c4(geometry, capi, oracle_mod):
+    bits = inputs.special_values_bf16()
+    if geometry == "reference":
+        check_against_oracle(capi, oracle_mod, bits, "bf16")
+    else:
+        check_against_oracle(capi, oracle_mod, bits, "bf16", 1000, 4064)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_special_values_every_nonfinite_pattern(dtype, capi, oracle_mod):
+    # every inf/NaN bit pattern of the dtype, each in its own block with
+    # random finite neighbours, plus zeros and subnormals in the same blocks
+    if dtype == "bf16":
+        pats = np.array([p | s for p in range(0x7F80, 0x8000) for s in (0, 0x8000)], np.uint16)
+        fin = inputs.normal(len(pats), 32, 99)
+    else:
+        pats = np.array([p | s for p in range(0x7C00, 0x8000) for s in (0, 0x8000)], np.uint16)
+        fin = inputs.normal(len(pats), 32, 99, "fp16")
+    bits = fin.copy()
+    idx = RNG.integers(0, 32, size=len(pats))
+    bits[np.arange(len(pats)), idx] = pats
+    bits[:, (idx + 7) % 32] = 0
+    bits[:, (idx + 11) % 32] = 0x8000
+    bits[:, (idx + 13) % 32] = 0x0003
+    check_against_oracle(capi, oracle_mod, bits, dtype)
+
+
+SHAPES = [(1, 1), (1, 32), (2, 64), (7, 33), (8, 256), (9, 255), (127, 129), (128, 128), (129, 4064),
+          (300, 8), (17, 1000), (256, 1024), (1000, 4064), (2051, 2080), (640, 4352), (1, 16384)]
+
+
+@pytest.mark.parametrize("m,k", SHAPES)
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_ragged_shapes_reference_geometry(m, k, dtype, capi, oracle_mod):
+    bits = inputs.normal(m, k, m * 7919 + k, dtype, sigma=3.0)
+    check_against_oracle(capi, oracle_mod, bits, dtype)
+
+
+@pytest.mark.parametrize("m,k", SHAPES)
+def test_ragged_shapes_tight_geometry(m, k, capi, oracle_mod):
+    bits = inputs.special_values_bf16(m, max(32, (k + 31) // 32 * 32), seed=m + k)[:, :k].copy()
+    check_against_oracle(capi, oracle_mod, bits, "bf16", m, (k + 31) // 32 * 32)
+
+
+@pytest.mark.parametrize("layout", ["x_ld_odd", "x_misaligned", "q_misaligned", "s_word_aligned_only",
+                                    "x_strided_tma", "q_strided"])
+def test_layouts_and_generic_path(layout, capi, oracle_mod):
+    bits = inputs.normal(333, 544, 5, "fp16")
+    kw = {}
+    if layout == "x_ld_odd":
+        kw = dict(ld_x=547)          # row stride not a multiple of 8 -> plain-load kernel
+    elif layout == "x_misaligned":
+        kw = dict(x_offset=1)        # 2-byte aligned only -> plain-load kernel
+    elif layout == "q_misaligned":
+        kw = dict(q_offset=3)
+    elif layout == "s_word_aligned_only":
+        kw = dict(s_offset=4)
+    elif layout == "x_strided_tma":
+        kw = dict(ld_x=1024)         # TMA with a row stride
+    elif layout == "q_strided":
+        kw = dict(ld_q=800)
+    check_against_oracle(capi, oracle_mod, bits, "fp16", 336, 544, **kw)
+
+
+def test_padded_entry_point_matches_general(capi, oracle_mod):
+    bits = inputs.normal(1024, 2048, 77)
+    x = torch.from_numpy(bits.view(np.int16)).cuda()
+    s_bytes = capi.scale_storage_bytes(1024, 2048)
+    q = torch.empty((1024, 2048), dtype=torch.uint8, device="cuda")
+    s = torch.empty((s_bytes // 4,), dtype=torch.int32, device="cuda")
+    capi.quantize_padded(x.data_ptr(), q.data_ptr(), s.data_ptr(), 1024, 2048, s_bytes // 4, 0,
+                         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    q_ref, s_ref = oracle_mod.quantize(bits, "bf16", 1024, 2048)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(s.cpu().numpy().view(np.uint8), s_ref)
+    with pytest.raises(ValueError):
+        capi.quantize_padded(x.data_ptr(), q.data_ptr(), s.data_ptr(), 1000, 2048, s_bytes // 4, 0, 0)
+
+
+@pytest.mark.slow
+def test_row_sharded_c5_shape_matches_unsharded(capi, oracle_mod):
+    """Config 5's 131072 x 16384 bf16 N(0, 2) matrix, quantized whole and as 8
+    row shards of 128-row chunks (one per GPU of an 8-GPU run): the shards'
+    Q and S are contiguous slices of the whole result, byte for byte.  A few
+    row chunks are also checked against the oracle."""
+    m, k = 131072, 16384
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = (torch.randn((m, k), generator=g, device="cuda", dtype=torch.float32) * 2.0).to(torch.bfloat16)
+    s_bytes = capi.scale_storage_bytes(m, k)
+    q = torch.empty((m, k), dtype=torch.uint8, device="cuda")
+    s = torch.empty((s_bytes,), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    capi.quantize(x.data_ptr(), 0, m, k, k, q.data_ptr(), m, k, k, s.data_ptr(), s_bytes, st)
+    rows = m // 8
+    per_s = capi.scale_storage_bytes(rows, k)
+    qs = torch.empty((rows, k), dtype=torch.uint8, device="cuda")
+    ss = torch.empty((per_s,), dtype=torch.uint8, device="cuda")
+    for r in range(8):
+        xr = x[r * rows:(r + 1) * rows]
+        capi.quantize(xr.data_ptr(), 0, rows, k, k, qs.data_ptr(), rows, k, k, ss.data_ptr(), per_s, st)
+        assert torch.equal(qs, q[r * rows:(r + 1) * rows])
+        assert torch.equal(ss, s[r * per_s:(r + 1) * per_s])
+    torch.cuda.synchronize()
+    chunk_bytes = capi.scale_storage_bytes(128, k)
+    for c in (0, 377, 1023):
+        xb = x[c * 128:(c + 1) * 128].view(torch.int16).cpu().numpy().view(np.uint16)
+        q_ref, s_ref = oracle_mod.quantize(xb, "bf16", 128, k)
+        assert np.array_equal(q[c * 128:(c + 1) * 128].cpu().numpy(), q_ref)
+        assert np.array_equal(s[c * chunk_bytes:(c + 1) * chunk_bytes].cpu().numpy(), s_ref)
+    del x, q, s
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_dequantize_matches_oracle(out_dtype, capi, oracle_mod):
+    import MXFP8_quantizer
+
+    pkg = MXFP8_quantizer.load_package()
+    bits = inputs.special_values_bf16(256, 1024, seed=8)
+    x = inputs.bits_to_torch(bits, "bf16").cuda()
+    q, s = pkg.quantize(x, q_rows=256, q_cols=1024)
+    y = pkg.dequantize(q, s, out_dtype)
+    torch.cuda.synchronize()
+    ref = oracle_mod.dequantize(q.view(torch.uint8).cpu().numpy(), s.cpu().numpy())
+    ref_t = torch.from_numpy(ref).to(out_dtype).float()
+    got = y.float().cpu()
+    both_nan = torch.isnan(got) & torch.isnan(ref_t)
+    assert torch.equal(torch.where(both_nan, 0.0, got), torch.where(both_nan, 0.0, ref_t))
+
+
+def test_drop_in_api_small(capi):
+    import MXFP8_quantizer
+
+    r = MXFP8_quantizer.run_quantizer(m=2051, k=2080, input_dtype="fp16", warmup_iterations=2, iterations=5,
+                                      benchmark_repeats=2)
+    assert r["verification_passed"] and r["q_max_byte_diff"] == 0 and r["scale_bytes_exact"]
+    assert r["kernel_m"] == 2056 and r["kernel_k"] == 2304 and r["runtime_min_us"] > 0
+    res = MXFP8_quantizer.prepare_and_quantize(1000, 4064, "bf16", 3, None)
+    assert res["kernel_k"] == 4096 and res["verify"]["q_max_byte_diff"] == 0
+    s = res["buffers"]["s_storage_bytes"].cpu().numpy()
+    pkg = MXFP8_quantizer.load_package()
+    dense = pkg.decode_scale_bytes(torch.from_numpy(s), 1024, 4096).numpy()
+    assert (dense[:1000, 127] == 127).all() and (dense[1000:] == 0).all()
+
+
+def test_cold_l2_benchmark_mode(capi):
+    import MXFP8_quantizer
+
+    r = MXFP8_quantizer.run_quantizer(m=4096, k=4096, warmup_iterations=2, iterations=4, benchmark_repeats=1,
+                                      cold_l2=True)
+    assert r["workspace_count"] > 1 and r["verification_passed"]
+
+
+@pytest.mark.parametrize("cfg", [(1024, 1024, 2048, "bf16", 0), (1024, 2048, 4096, "fp16", 2)])
+def test_e2e_blockscaled_gemm(cfg, capi):
+    import MXFP8_quantizer
+
+    m, n, k, dt, seed = cfg
+    r = MXFP8_quantizer.run_e2e_verification(m=m, n=n, k=k, input_dtype=dt, seed=seed)
+    assert r["e2e_verification_passed"] and r["max_err_ratio"] < 1.0
+
+
+def test_status_word_clean(capi):
+    assert capi.device_status(clear=False) == 0
