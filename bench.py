@@ -185,6 +185,44 @@ def reference_arm(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+SIDE_BY_SIDE = [
+    # (m, k, dtype, cold_l2): BASELINE config 2 and the reference README's table
+    (8192, 8192, "bf16", False), (8192, 8192, "bf16", True), (16384, 16384, "bf16", False),
+    (16384, 16384, "fp16", False), (32768, 16384, "bf16", False), (32768, 8192, "bf16", False),
+    (16384, 16384, "bf16", True), (16385, 16384, "bf16", False), (2051, 2080, "fp16", False),
+    (2048, 2048, "bf16", False), (16384, 4096, "fp16", False),
+]
+
+
+def reference_kernel_arm(args, rank: int) -> None:
+    """The reference's CuTeDSL kernel and this library, each through its own
+    run_quantizer (same timing rule: min over 5 passes of the mean of 50
+    launches after 10 warm-up launches), on the same GPU.  Needs the
+    reference module; prints one JSON line per configuration."""
+    if rank != 0:
+        return
+    import importlib.util
+
+    import torch
+
+    import MXFP8_quantizer
+
+    spec = importlib.util.spec_from_file_location("reference_mxfp8_quantizer",
+                                                  pathlib.Path(args.reference_path) / "MXFP8_quantizer.py")
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    ours = MXFP8_quantizer.load_package()
+    for m, k, dt, cold in SIDE_BY_SIDE:
+        row = {"m": m, "k": k, "input_dtype": dt, "cold_l2": cold, "device": torch.cuda.get_device_name(0)}
+        for name, fn in (("reference_cutedsl", ref.run_quantizer), ("b200", ours.run_quantizer)):
+            r = fn(m=m, k=k, input_dtype=dt, warmup_iterations=10, iterations=50, benchmark_repeats=5, cold_l2=cold)
+            row[name] = {key: r[key] for key in ("effective_tb_s", "runtime_min_us", "runtime_std_us",
+                                                 "verification_passed", "q_max_byte_diff", "workspace_count")}
+            torch.cuda.empty_cache()
+        row["speedup"] = row["b200"]["effective_tb_s"] / row["reference_cutedsl"]["effective_tb_s"]
+        print(json.dumps(row), flush=True)
+
+
 def cpu_model() -> str:
     try:
         for ln in open("/proc/cpuinfo"):
@@ -208,7 +246,9 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=4000)
     ap.add_argument("--warmup", type=int, default=50)
-    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--impl", choices=["b200", "reference", "reference-kernel"], default="b200")
+    ap.add_argument("--reference-path", default=str(ROOT / "baseline" / "_ref"),
+                    help="directory holding the reference's MXFP8_quantizer.py (reference-kernel arm)")
     ap.add_argument("--m", type=int, default=M_DEFAULT)
     ap.add_argument("--k", type=int, default=K_DEFAULT)
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -223,6 +263,9 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.impl == "reference-kernel":
+        reference_kernel_arm(args, rank)
         return
 
     import torch

@@ -89,8 +89,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     quantize_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap qmap,
                         const TmaParams p) {
     using L = Layout<STAGES>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // Pointer arithmetic on the __shared__ array (not integer casts) keeps the
+    // accesses below plain LDS/STS instead of generic loads and stores.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t full0 = sbase + L::bar_off;
     const uint32_t empty0 = full0 + STAGES * 8;

@@ -308,12 +308,10 @@ def check_cuda_launch_errors(stream=None, context: str = "kernel launch") -> Non
     """Synchronise the stream and surface device errors, including the
     library's sticky device status word (bounded pipeline waits)."""
     try:
-        if stream is None:
-            torch.cuda.current_stream().synchronize()
-        elif isinstance(stream, torch.cuda.Stream):
+        if isinstance(stream, torch.cuda.Stream):
             stream.synchronize()
         else:
-            torch.cuda.ExternalStream(int(stream)).synchronize()
+            torch.cuda.synchronize()
     except RuntimeError as exc:  # surfaced by the CUDA runtime
         raise RuntimeError(f"CUDA error after {context}: {exc}") from exc
     status = _capi.device_status(clear=True)
@@ -420,14 +418,16 @@ def _l2_bytes() -> int:
     return int(torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size)
 
 
-def benchmark_compiled_quantizer(launch, stream: int, warmup: int, iters: int, workspaces: list, repeats: int):
+def benchmark_compiled_quantizer(launch, stream: torch.cuda.Stream, warmup: int, iters: int, workspaces: list,
+                                 repeats: int):
     """min/mean/std over `repeats` passes of: `warmup` launches, then CUDA
     events around `iters` launches, mean per launch (the timing rule of
-    MXFP8_quantizer.py:730-761 and the CuTeDSL testing.benchmark it calls)."""
+    MXFP8_quantizer.py:730-761 and the CuTeDSL testing.benchmark it calls).
+    The events are recorded on `stream`, the stream the launches use."""
     samples_us = []
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    ext = torch.cuda.ExternalStream(stream)
+    ext = stream
     n = len(workspaces)
     for _ in range(repeats):
         idx = 0
@@ -458,7 +458,8 @@ def run_quantizer(m: int = 16384, k: int = 16384, rows_per_cta: int = DEFAULT_RO
     cfg = MXFP8QuantizerConfig(torch_dtype, rows_per_cta, k_tile)
     cfg.validate()
     x = torch.randn((m, k), dtype=torch_dtype, device="cuda")
-    stream = torch.cuda.current_stream().cuda_stream
+    stream_obj = torch.cuda.current_stream()
+    stream = stream_obj.cuda_stream
     is_full_tile = (m % rows_per_cta == 0) and (k % k_tile == 0)
     kernel_m, kernel_k, grid_m, grid_k = shape_problem(m, k, rows_per_cta, k_tile)
     buffers = materialize_quantizer_buffers(kernel_m, kernel_k, torch_dtype, x)
@@ -504,7 +505,7 @@ def run_quantizer(m: int = 16384, k: int = 16384, rows_per_cta: int = DEFAULT_RO
         flush = torch.empty(_l2_bytes() * 2 // 4, dtype=torch.int32, device="cuda")
         flush.zero_()
         del flush
-    timing = benchmark_compiled_quantizer(compiled, stream, warmup_iterations, iterations, workspaces,
+    timing = benchmark_compiled_quantizer(compiled, stream_obj, warmup_iterations, iterations, workspaces,
                                           benchmark_repeats)
     check_cuda_launch_errors(stream, "quantizer benchmark")
     rmin, rmean, rstd = timing["min_runtime_s"], timing["mean_runtime_s"], timing["std_runtime_s"]

@@ -160,3 +160,23 @@ CONFIGS = {
     "c3": ("16384x4096 fp16 Student-t(3) + outliers seed 3", lambda: llm_activation_fp16(), "fp16"),
     "c4": ("1000x4064 bf16 log-uniform + specials seed 2", lambda: special_values_bf16(), "bf16"),
 }
+
+
+def nonfinite_patterns(dtype: str, seed: int = 99) -> np.ndarray:
+    """Every inf/NaN bit pattern of the dtype (both signs), one per 32-wide
+    row, among N(0,1) neighbours plus a +0, a -0 and a subnormal in the same
+    block (exercises 0*inf, -0 under a negative inverse scale, and tiny
+    values under a huge one)."""
+    if dtype == "bf16":
+        pats = np.array([p | s for p in range(0x7F80, 0x8000) for s in (0, 0x8000)], np.uint16)
+    else:
+        pats = np.array([p | s for p in range(0x7C00, 0x8000) for s in (0, 0x8000)], np.uint16)
+    bits = normal(len(pats), 32, seed, dtype)
+    rng = np.random.default_rng(seed)
+    idx = rng.integers(0, 32, size=len(pats))
+    rows = np.arange(len(pats))
+    bits[rows, (idx + 7) % 32] = 0
+    bits[rows, (idx + 11) % 32] = 0x8000
+    bits[rows, (idx + 13) % 32] = 0x0003
+    bits[rows, idx] = pats
+    return bits

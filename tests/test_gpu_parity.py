@@ -93,6 +93,22 @@ def test_reference_digests(name, capi, golden):
     assert sha(s) == rec["s_sha256"], f"{name}: packed scales differ from the reference recipe"
 
 
+@pytest.mark.parametrize("name", ["c4", "c4_ragged", "nonfinite_bf16", "nonfinite_fp16", "c1", "c2"])
+def test_reference_kernel_digests(name, capi):
+    """Bit-exact against the reference's CuTeDSL kernel run on a B200
+    (tests/golden/make_kernel_golden.py), special values included."""
+    import json
+    import pathlib
+
+    from make_kernel_golden import KERNEL_CASES
+
+    rec = json.loads((pathlib.Path(__file__).parent / "golden" / "golden_kernel.json").read_text())["cases"][name]
+    desc, gen, dtype = KERNEL_CASES[name]
+    q, s = gpu_quantize(capi, gen(), dtype, rec["kernel_m"], rec["kernel_k"])
+    assert sha(q) == rec["q_sha256"], f"{name}: payload differs from the reference kernel"
+    assert sha(s) == rec["s_sha256"], f"{name}: packed scales differ from the reference kernel"
+
+
 @pytest.mark.parametrize("geometry", ["reference", "tight"])
 def test_special_values_c4(geometry, capi, oracle_mod):
     bits = inputs.special_values_bf16()
@@ -104,21 +120,7 @@ def test_special_values_c4(geometry, capi, oracle_mod):
 
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 def test_special_values_every_nonfinite_pattern(dtype, capi, oracle_mod):
-    # every inf/NaN bit pattern of the dtype, each in its own block with
-    # random finite neighbours, plus zeros and subnormals in the same blocks
-    if dtype == "bf16":
-        pats = np.array([p | s for p in range(0x7F80, 0x8000) for s in (0, 0x8000)], np.uint16)
-        fin = inputs.normal(len(pats), 32, 99)
-    else:
-        pats = np.array([p | s for p in range(0x7C00, 0x8000) for s in (0, 0x8000)], np.uint16)
-        fin = inputs.normal(len(pats), 32, 99, "fp16")
-    bits = fin.copy()
-    idx = RNG.integers(0, 32, size=len(pats))
-    bits[np.arange(len(pats)), idx] = pats
-    bits[:, (idx + 7) % 32] = 0
-    bits[:, (idx + 11) % 32] = 0x8000
-    bits[:, (idx + 13) % 32] = 0x0003
-    check_against_oracle(capi, oracle_mod, bits, dtype)
+    check_against_oracle(capi, oracle_mod, inputs.nonfinite_patterns(dtype), dtype)
 
 
 SHAPES = [(1, 1), (1, 32), (2, 64), (7, 33), (8, 256), (9, 255), (127, 129), (128, 128), (129, 4064),
@@ -171,7 +173,7 @@ def test_padded_entry_point_matches_general(capi, oracle_mod):
     assert np.array_equal(q.cpu().numpy(), q_ref)
     assert np.array_equal(s.cpu().numpy().view(np.uint8), s_ref)
     with pytest.raises(ValueError):
-        capi.quantize_padded(x.data_ptr(), q.data_ptr(), s.data_ptr(), 1000, 2048, s_bytes // 4, 0, 0)
+        capi.quantize_padded(x.data_ptr(), q.data_ptr(), s.data_ptr(), 1001, 2048, s_bytes // 4, 0, 0)
 
 
 @pytest.mark.slow

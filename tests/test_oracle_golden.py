@@ -2,13 +2,18 @@
 
 The golden digests in tests/golden/golden.json were produced by the
 reference's torch restatement (MXFP8_quantizer.py:610-662); see
-tests/golden/make_golden.py.  Special-value blocks are checked against
-known answers derived from the PTX definitions of the reference kernel's
-instructions (MXFP8_quantizer.py:116-200, 473-501).
+tests/golden/make_golden.py.  tests/golden/golden_kernel.json holds digests
+of the reference's CuTeDSL kernel itself, run on a B200
+(tests/golden/make_kernel_golden.py), which pin the inf/NaN semantics too.
+Special-value blocks are also checked against known answers derived from
+the PTX definitions of the reference kernel's instructions
+(MXFP8_quantizer.py:116-200, 473-501).
 """
 
 import base64
 import hashlib
+import json
+import pathlib
 import struct
 import zlib
 from fractions import Fraction
@@ -230,3 +235,19 @@ def test_dequantize_roundtrip_bound(oracle_mod):
     scale = np.repeat(np.exp2(oracle_mod.unpack_scales(s, 64, 8).astype(np.float32) - 127), 32, axis=1)
     err = np.abs(y - x)
     assert (err <= np.maximum(np.abs(x) * 2.0 ** -4, scale * 2.0 ** -10) + 1e-30).all()
+
+
+KERNEL_GOLDEN = json.loads((pathlib.Path(__file__).resolve().parent / "golden" / "golden_kernel.json").read_text())
+
+
+@pytest.mark.parametrize("name", [n for n in KERNEL_GOLDEN["cases"] if n not in ("c2", "c3")])
+def test_oracle_matches_reference_kernel_digests(name, oracle_mod):
+    """The reference's CuTeDSL kernel itself, run on a B200 (make_kernel_golden.py),
+    including every inf/NaN pattern and the special-value config."""
+    from make_kernel_golden import KERNEL_CASES
+
+    rec = KERNEL_GOLDEN["cases"][name]
+    desc, gen, dtype = KERNEL_CASES[name]
+    q, s = oracle_mod.quantize(gen(), dtype, rec["kernel_m"], rec["kernel_k"])
+    assert sha(q) == rec["q_sha256"], f"payload differs from the reference kernel on {name}"
+    assert sha(s) == rec["s_sha256"], f"packed scales differ from the reference kernel on {name}"
