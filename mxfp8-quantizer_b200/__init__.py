@@ -3,7 +3,7 @@ the tcgen05 128x4 chunk layout.  The compute runs in libmxfp8.so (sm_100a
 CUDA, C ABI in include/mxfp8.h); this package is the Python host side that
 mirrors the reference's API (see quantizer.py)."""
 
-from . import _capi
+from . import _capi, shard
 from .quantizer import (
     DEFAULT_E2E_SUITE,
     DEFAULT_K_TILE,
