@@ -80,6 +80,29 @@ MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int64_t k, int
                    void* q, int64_t q_rows, int64_t q_cols, int64_t ld_q,
                    void* s, int64_t s_bytes, mxfp8_stream_t stream);
 
+/* Allocation-free variant of mxfp8_quantize: same arguments, checks,
+ * kernels and output bytes, but no call ever allocates device memory.
+ * No counterpart in the reference.
+ * Who needs it: callers that may not call cudaMalloc.  mxfp8_quantize
+ * allocates a 256-byte status buffer on its first call on each device, which
+ * fails or is forbidden for code that runs while a CUDA graph is being
+ * captured, for plugins whose host owns all device memory through its own
+ * pool or arena, and on a device whose memory another allocator has already
+ * reserved in full.
+ * How: the quantize kernel's only scratch, one 32-bit status word written
+ * when a pipeline wait times out, lives in a fixed 256-byte device array of
+ * the library (64 words; every GPU that loads the library holds it until
+ * exit).  A call needs 1 word, so no problem size exceeds the array.  The
+ * first call on each device looks up the array's device address (no
+ * allocation); make that first call before any stream capture.  Each call
+ * clears the word in stream order before its kernel runs.  All calls share
+ * the array, so calls whose kernels overlap on the GPU (different streams)
+ * race on that word; its contents are not readable through this API
+ * (mxfp8_device_status reports only the mxfp8_quantize word). */
+MXFP8_API int mxfp8_quantize_noalloc(const void* x, int dtype, int64_t m, int64_t k, int64_t ld_x,
+                                     void* q, int64_t q_rows, int64_t q_cols, int64_t ld_q,
+                                     void* s, int64_t s_bytes, mxfp8_stream_t stream);
+
 /* Reference-compatible launch on already padded, contiguous buffers: x and q
  * are (m, k) with m % 8 == 0 and k % 256 == 0 (the reference's launch shape),
  * s holds s_word_count 32-bit words (>= the packed storage of (m, k)).

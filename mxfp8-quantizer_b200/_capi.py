@@ -33,6 +33,7 @@ EXPORTS = (
     "mxfp8_scale_storage_bytes",
     "mxfp8_launch_shape",
     "mxfp8_quantize",
+    "mxfp8_quantize_noalloc",
     "mxfp8_quantize_padded",
     "mxfp8_dequantize",
     "mxfp8_device_status",
@@ -67,6 +68,8 @@ def lib() -> ctypes.CDLL:
         L.mxfp8_launch_shape.restype = i32
         L.mxfp8_quantize.argtypes = [vp, i32, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp]
         L.mxfp8_quantize.restype = i32
+        L.mxfp8_quantize_noalloc.argtypes = [vp, i32, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp]
+        L.mxfp8_quantize_noalloc.restype = i32
         L.mxfp8_quantize_padded.argtypes = [vp, vp, vp, i64, i64, i64, i32, vp]
         L.mxfp8_quantize_padded.restype = i32
         L.mxfp8_dequantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, i64, vp]
@@ -115,6 +118,15 @@ def quantize(x_ptr: int, dtype: int, m: int, k: int, ld_x: int, q_ptr: int, q_ro
     rc = lib().mxfp8_quantize(x_ptr or None, dtype, m, k, ld_x, q_ptr or None, q_rows, q_cols, ld_q,
                               s_ptr or None, s_bytes, stream or None)
     check(rc, "quantizer launch")
+
+
+def quantize_noalloc(x_ptr: int, dtype: int, m: int, k: int, ld_x: int, q_ptr: int, q_rows: int, q_cols: int,
+                     ld_q: int, s_ptr: int, s_bytes: int, stream: int) -> None:
+    """mxfp8_quantize_noalloc: like quantize(), but the library never allocates
+    device memory (for callers that may not call cudaMalloc)."""
+    rc = lib().mxfp8_quantize_noalloc(x_ptr or None, dtype, m, k, ld_x, q_ptr or None, q_rows, q_cols, ld_q,
+                                      s_ptr or None, s_bytes, stream or None)
+    check(rc, "quantizer launch (allocation-free)")
 
 
 def quantize_padded(x_ptr: int, q_ptr: int, s_ptr: int, m: int, k: int, s_word_count: int, dtype: int,

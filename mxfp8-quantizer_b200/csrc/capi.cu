@@ -141,6 +141,60 @@ extern "C" MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int
     return tma_ok ? launch_quantize_tma(a, dev->sm_count, st) : launch_quantize_generic(a, dev->sm_count, st);
 }
 
+// Allocation-free entry: the same argument checks and kernels as
+// mxfp8_quantize, but device properties come from attribute queries and the
+// kernel's scratch word lives in a fixed device array (quantize_tma.cu), so
+// no call, first or later, allocates device memory.
+extern "C" MXFP8_API int mxfp8_quantize_noalloc(const void* x, int dtype, int64_t m, int64_t k, int64_t ld_x,
+                                               void* q, int64_t q_rows, int64_t q_cols, int64_t ld_q, void* s,
+                                               int64_t s_bytes, mxfp8_stream_t stream) {
+    if (dtype != MXFP8_BF16 && dtype != MXFP8_FP16) return MXFP8_ERR_DTYPE;
+    if (m < 0 || k < 0 || q_rows < m || q_cols < k || q_cols % 32 != 0 || ld_x < k || ld_q < q_cols ||
+        q_rows > kInt32Max || q_cols > kInt32Max || ld_x > (int64_t(1) << 38) || ld_q > (int64_t(1) << 39))
+        return MXFP8_ERR_SHAPE;
+    if (q_rows == 0 || q_cols == 0) return MXFP8_OK;
+    const bool has_x = m > 0 && k > 0;
+    if (!q || !s || (has_x && !x)) return MXFP8_ERR_NULL_POINTER;
+    if ((has_x && !aligned(x, 2)) || !aligned(s, 4)) return MXFP8_ERR_ALIGNMENT;
+    if (s_bytes < mxfp8_scale_storage_bytes(q_rows, q_cols)) return MXFP8_ERR_SCALE_BUFFER;
+
+    QuantizeArgs a;
+    a.x = x;
+    a.dtype = dtype;
+    a.m = m;
+    a.k = k;
+    a.ld_x = ld_x;
+    a.q = static_cast<uint8_t*>(q);
+    a.q_rows = q_rows;
+    a.q_cols = q_cols;
+    a.ld_q = ld_q;
+    a.s = static_cast<uint8_t*>(s);
+    a.scale_rows = ceil_div(q_rows, 128) * 128;
+    a.scale_cols = q_cols / 32;
+    a.col_chunks = ceil_div(a.scale_cols, 4);
+    a.status = nullptr;
+    if ((a.scale_rows / 128) * a.col_chunks > kInt32Max) return MXFP8_ERR_SHAPE;
+
+    int dev = -1, sms = 0, major = 0, minor = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess) {
+        set_last_error("device query", (int)e);
+        return MXFP8_ERR_DEVICE;
+    }
+    if (major != 10 || minor != 0) {
+        set_last_error("libmxfp8 is built for sm_100a (B200); the current device is another architecture", 0);
+        return MXFP8_ERR_DEVICE;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool tma_ok = has_x && aligned(x, 16) && ld_x % 8 == 0 && aligned(q, 16) && ld_q % 16 == 0 &&
+                        aligned(s, 16);
+    // The plain-load kernel uses no scratch, so it runs unchanged.
+    return tma_ok ? launch_quantize_tma_noalloc(a, dev, sms, st) : launch_quantize_generic(a, sms, st);
+}
+
 extern "C" MXFP8_API int mxfp8_quantize_padded(const void* x, void* q_dwords, void* s_words, int64_t m, int64_t k,
                                      int64_t s_word_count, int dtype, mxfp8_stream_t stream) {
     if (m < 1 || k < 1 || m % 8 != 0 || k % 256 != 0 || s_word_count < 0) return MXFP8_ERR_SHAPE;

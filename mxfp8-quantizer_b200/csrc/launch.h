@@ -23,6 +23,8 @@ struct QuantizeArgs {
 // Returned by launchers: 0, or a negative mxfp8_status.
 int launch_quantize_tma(const QuantizeArgs& a, int sm_count, cudaStream_t stream);
 int launch_quantize_generic(const QuantizeArgs& a, int sm_count, cudaStream_t stream);
+// Same kernel as launch_quantize_tma, scratch in a fixed device array (never allocates).
+int launch_quantize_tma_noalloc(const QuantizeArgs& a, int dev, int sm_count, cudaStream_t stream);
 int launch_dequantize(const uint8_t* q, int64_t rows, int64_t cols, int64_t ld_q, const uint8_t* s,
                       void* out, int out_dtype, int64_t ld_out, cudaStream_t stream);
 

@@ -314,4 +314,59 @@ int launch_quantize_tma(const QuantizeArgs& a, int sm_count, cudaStream_t stream
                             : launch_tma_typed<kFP16>(a, sm_count, stream);
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free launch.  The kernel above needs one word of global scratch
+// (its status word for bounded-wait timeouts).  mxfp8_quantize keeps that
+// word in a buffer it allocates on the first call on each device; this
+// variant keeps it in a fixed device array of this file instead, so it never
+// allocates.  Every GPU that loads the library holds the array until exit.
+// ---------------------------------------------------------------------------
+
+constexpr int kNoAllocScratchWords = 64;  // 256 bytes per device
+constexpr int kStatusWordsPerCall = 1;
+constexpr int kMaxNoAllocDevices = 64;
+static __device__ __align__(256) unsigned int g_noalloc_scratch[kNoAllocScratchWords];
+
+static std::mutex g_noalloc_mu;
+static unsigned int* g_noalloc_addr[kMaxNoAllocDevices];
+
+// Device address of g_noalloc_scratch on device `dev` (the current device),
+// looked up once per device.  In host code the array's name is only a
+// host-side stand-in; the kernel must be given this address.
+static int noalloc_scratch(int dev, unsigned int** out) {
+    if (dev < 0 || dev >= kMaxNoAllocDevices) {
+        set_last_error("device index beyond the allocation-free table", 0);
+        return MXFP8_ERR_DEVICE;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr) {
+            set_last_error("cudaGetSymbolAddress(g_noalloc_scratch)", (int)e);
+            return MXFP8_ERR_CUDA;
+        }
+        g_noalloc_addr[dev] = static_cast<unsigned int*>(ptr);
+    }
+    *out = g_noalloc_addr[dev];
+    return MXFP8_OK;
+}
+
+int launch_quantize_tma_noalloc(const QuantizeArgs& args, int dev, int sm_count, cudaStream_t stream) {
+    static_assert(kStatusWordsPerCall <= kNoAllocScratchWords, "scratch array too small");
+    unsigned int* scratch = nullptr;
+    int rc = noalloc_scratch(dev, &scratch);
+    if (rc) return rc;
+    // The array keeps the previous call's contents: the status word must
+    // start at zero, so clear it in stream order before the kernel runs.
+    cudaError_t e = cudaMemsetAsync(scratch, 0, kStatusWordsPerCall * sizeof(unsigned int), stream);
+    if (e != cudaSuccess) {
+        set_last_error("cudaMemsetAsync(scratch)", (int)e);
+        return MXFP8_ERR_CUDA;
+    }
+    QuantizeArgs a = args;
+    a.status = scratch;
+    return launch_quantize_tma(a, sm_count, stream);
+}
+
 }  // namespace mxfp8
