@@ -66,6 +66,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue now, and wait until the previous kernel's grid has completed and
+// its memory is visible.  Both are no-ops for a plain launch.
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_wait_prerequisites() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 2-D TMA tile store shared -> global (bulk-group completion); the tensor
 // map's bounds clip the tile at the matrix edge.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t x, int32_t y, uint32_t src) {
