@@ -1,5 +1,5 @@
-// ptx.cuh -- hand-written PTX wrappers for sm_100a: mbarriers, TMA tile
-// loads/stores, bulk copies, async-proxy fences, named barriers.
+// ptx.cuh -- hand-written PTX wrappers for sm_100a: mbarriers with bounded
+// waits, TMA tile loads, tensor-map prefetch, programmatic dependent launch.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
@@ -66,6 +66,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// L2 prefetch of one 2-D TMA box (no shared memory, no completion).  Only a
+// hint: L2 is where every global write lands, so a later load still sees the
+// latest data even if the lines were prefetched before it was written.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue now, and wait until the previous kernel's grid has completed and
 // its memory is visible.  Both are no-ops for a plain launch.
@@ -74,64 +84,8 @@ __device__ __forceinline__ void grid_launch_dependents() {
 }
 __device__ __forceinline__ void grid_wait_prerequisites() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// 2-D TMA tile store shared -> global (bulk-group completion); the tensor
-// map's bounds clip the tile at the matrix edge.
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t x, int32_t y, uint32_t src) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y), "r"(src)
-                 : "memory");
-}
-
-// Linear bulk copy shared -> global; both addresses 16-byte aligned, size a
-// multiple of 16.
-__device__ __forceinline__ void bulk_store(void* gdst, uint32_t src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(src),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
-template <int N>
-__device__ __forceinline__ void bulk_wait_all() {
-    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// Make this thread's generic-proxy shared-memory writes visible to the
-// async proxy (TMA / bulk copies issued afterwards).
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-    uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(addr));
-    return v;
-}
-
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
-                 : "memory");
-}
-
-__device__ __forceinline__ void sts16(uint32_t addr, uint16_t v) {
-    asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
 }
 
 }  // namespace mxfp8

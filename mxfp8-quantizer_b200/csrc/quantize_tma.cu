@@ -4,26 +4,34 @@
 // chunk of the packed scale layout (128 rows x 4 scale columns).  One CTA per
 // SM walks tiles round-robin.  Warp 8 (one elected lane) streams X tiles into
 // a 3-deep shared-memory ring with 2-D TMA loads (two 64-column boxes,
-// 128-byte swizzle, zero fill outside (m, k)); warps 0-7 compute; finished
-// payload tiles and scale chunks leave through a TMA tile store and a bulk
-// copy from one of two staging buffers, so global stores are full-line and
-// asynchronous.  One reduction barrier per tile among the 256 compute
-// threads both publishes the staging buffer and agrees on aborting.
+// 128-byte swizzle, zero fill outside (m, k)); warps 0-7 compute into one of
+// two staging buffers (payload tile + 512-byte scale chunk); one reduction
+// barrier per tile among the 256 compute threads publishes the buffer and
+// agrees on aborting; then each compute warp writes 16 payload rows back with
+// 16-byte streaming stores, 8 lanes per 128-byte row, so every store
+// instruction writes four whole lines, and warp 0 writes the scale chunk.
 //
-// Depth: 3 stages (96 KiB of X in flight per SM, ~14 MB on the GPU) measured
-// faster than 4 or 5 on B200 (6.0-6.2 vs 5.6 TB/s at 16384^2): more
-// outstanding loads only crowd out the payload write-back.
+// Measured on B200 (min over runs, TB/s at 16384^2 / 8192^2): these plain
+// coalesced stores beat TMA tile stores of the same staging buffer
+// (6.6 vs 6.1-6.4 / 6.19 vs 6.12), and 3 stages (96 KiB of X in flight per
+// SM) beat 2, 4 and 5: more outstanding loads crowd out the write-back.
 //
 // Launch: programmatic dependent launch.  Each CTA lets the next kernel in
-// the stream start its prologue as soon as SMs free up, and itself touches
-// global memory only after griddepcontrol.wait, i.e. after the previous
-// kernel has completed; back to back this hides ~1.7 us per launch.
+// the stream start its prologue as soon as SMs free up, asks L2 to prefetch
+// its first two X tiles, and only then waits (griddepcontrol.wait) for the
+// previous kernel to complete before any load or store of its own.  The
+// prefetch is a hint (no data moves into the CTA before the wait), so it is
+// safe even when the previous kernel writes X; it fills the DRAM bubble
+// between back-to-back launches: 8192^2 went from 5.83 (plain launch) to
+// 6.16 (dependent launch) to 6.63 TB/s (plus the prefetch).
 //
 // Thread map inside a tile: thread t handles row (t % 128) and the two
 // scale blocks 2*(t/128) and 2*(t/128)+1, i.e. 64 contiguous input values
 // that sit in box (t/128).  Within an 8-lane shared-memory phase the rows
 // are consecutive, so the 128-byte swizzle makes every 16-byte access
-// conflict-free, for the X reads and for the payload writes alike.
+// conflict-free, for the X reads and for the payload writes alike; the
+// store pass reads the 8 chunks of one row per 8-lane phase, also
+// conflict-free.
 //
 // Reference behaviour restated (not its structure): MXFP8_quantizer.py:355-525.
 #include <cuda.h>
@@ -50,6 +58,7 @@ constexpr int kComputeWarps = 8;
 constexpr int kComputeThreads = kComputeWarps * 32;
 constexpr int kThreads = kComputeThreads + 32;            // + producer warp
 constexpr int kQBufs = 2;
+constexpr int kPrefetchTiles = 2;                        // L2 prefetch before the dependency wait
 constexpr uint64_t kWaitLimitNs = 1000000000ull;          // 1 s per pipeline wait
 constexpr uint32_t kBarCompute = 1;                       // named barrier id
 
@@ -67,9 +76,12 @@ struct Layout {
 };
 
 struct TmaParams {
+    uint8_t* q;
+    int64_t ld_q;
+    int q_rows;
+    int q_cols;
     int n_tiles;
     int n_col_tiles;
-    int q_rows;
     int scale_cols;
     int col_chunks;
     uint8_t* s;
@@ -95,8 +107,7 @@ __device__ __forceinline__ void report(unsigned int* status, unsigned code) {
 
 template <int DT, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
-    quantize_tma_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap qmap,
-                        const TmaParams p) {
+    quantize_tma_kernel(const __grid_constant__ CUtensorMap xmap, const TmaParams p) {
     using L = Layout<STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // Pointer arithmetic on the __shared__ array (not integer casts) keeps the
@@ -120,13 +131,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         ctl[1] = 0;
         fence_mbar_init();
     }
-    if (tid == kComputeThreads) {
-        prefetch_tensormap(&xmap);
-        prefetch_tensormap(&qmap);
-    }
+    if (tid == kComputeThreads) prefetch_tensormap(&xmap);
     __syncthreads();
-    // Nothing above touched global memory; everything below may read X that
-    // the previous kernel wrote or overwrite Q/S that it reads.
+    if (tid == kComputeThreads) {
+        for (int i = 0, t = blockIdx.x; i < kPrefetchTiles && t < p.n_tiles; ++i, t += gridDim.x) {
+            const int rt = t / p.n_col_tiles;
+            const int ct = t - rt * p.n_col_tiles;
+            tma_prefetch_l2_2d(&xmap, ct * kTileCols, rt * kTileRows);
+            tma_prefetch_l2_2d(&xmap, ct * kTileCols + kBoxCols, rt * kTileRows);
+        }
+    }
+    // Nothing above loaded or stored global data; everything below may read X
+    // that the previous kernel wrote or overwrite Q/S that it reads.
     grid_launch_dependents();
     grid_wait_prerequisites();
 
@@ -209,11 +225,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (sc + 1 >= p.scale_cols) b1 = 0;
                 *reinterpret_cast<uint16_t*>(smem + L::s_off + qb * kSChunkBytes + (r & 31) * 16 + (r >> 5) * 4 +
                                              2 * h) = static_cast<uint16_t>(b0 | (b1 << 8));
-                fence_proxy_async_smem();
             }
-            // The store issued one tile ago must have finished reading its
-            // staging buffer before anyone writes that buffer next iteration.
-            if (tid == 0) bulk_wait_read<kQBufs - 2>();
+            // Publishes staging buffer qb.  Buffer qb is written again two
+            // tiles later, after the next barrier, which every thread reaches
+            // only once its stores below have read the buffer.
             if (bar_red_or(kBarCompute, kComputeThreads, !ok)) {
                 if (tid == 0) {
                     report(p.status, kErrTileWait);
@@ -221,17 +236,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 break;
             }
-            if (tid == 0) {
-                tma_store_2d(&qmap, ct * kTileCols, rt * kTileRows, sbase + L::q_off + qb * kQTileBytes);
-                bulk_store(p.s + ((int64_t)rt * p.col_chunks + ct) * kSChunkBytes,
-                           sbase + L::s_off + qb * kSChunkBytes, kSChunkBytes);
-                bulk_commit();
+            const uint8_t* qbuf = smem + L::q_off + qb * kQTileBytes;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int row = warp * 16 + i * 4 + (lane >> 3);
+                const int chunk = lane & 7;
+                const uint4 v = *reinterpret_cast<const uint4*>(qbuf + row * 128 + ((chunk ^ (row & 7)) << 4));
+                const int grow = rt * kTileRows + row;
+                const int col = ct * kTileCols + chunk * 16;  // q_cols % 32 == 0: a chunk is all in or all out
+                if (grow < p.q_rows && col < p.q_cols)
+                    __stcs(reinterpret_cast<uint4*>(p.q + (int64_t)grow * p.ld_q + col), v);
+            }
+            if (warp == 0) {
+                const uint4 v = *reinterpret_cast<const uint4*>(smem + L::s_off + qb * kSChunkBytes + lane * 16);
+                __stcs(reinterpret_cast<uint4*>(p.s + ((int64_t)rt * p.col_chunks + ct) * kSChunkBytes + lane * 16), v);
             }
         }
         if (tid == 0) ctl[1] = it;
     }
     __syncthreads();
-    if (tid == 0) bulk_wait_all<0>();
     if (warp == kComputeWarps && lane == 0) {
         // Loads issued but never consumed (only after an abort) still target
         // this CTA's shared memory: wait for them, with a limit, before exit.
@@ -295,19 +318,19 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
         set_last_error("cudaFuncSetAttribute", (int)e);
         return MXFP8_ERR_CUDA;
     }
-    CUtensorMap xmap, qmap;
+    CUtensorMap xmap;
     int rc = encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.x, (uint64_t)a.k, (uint64_t)a.m,
                        (uint64_t)a.ld_x * 2, kBoxCols, kTileRows);
-    if (rc) return rc;
-    rc = encode_2d(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.q, (uint64_t)a.q_cols, (uint64_t)a.q_rows,
-                   (uint64_t)a.ld_q, kTileCols, kTileRows);
     if (rc) return rc;
     TmaParams p;
     const int64_t n_row_tiles = a.scale_rows / kTileRows;
     const int64_t n_tiles = n_row_tiles * a.col_chunks;
     p.n_tiles = (int)n_tiles;
     p.n_col_tiles = (int)a.col_chunks;
+    p.q = a.q;
+    p.ld_q = a.ld_q;
     p.q_rows = (int)a.q_rows;
+    p.q_cols = (int)a.q_cols;
     p.scale_cols = (int)a.scale_cols;
     p.col_chunks = (int)a.col_chunks;
     p.s = a.s;
@@ -323,7 +346,7 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kernel, xmap, qmap, p);
+    e = cudaLaunchKernelEx(&cfg, kernel, xmap, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_last_error("quantize_tma_kernel launch", (int)e);

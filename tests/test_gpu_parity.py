@@ -261,3 +261,31 @@ def test_e2e_blockscaled_gemm(cfg, capi):
 
 def test_status_word_clean(capi):
     assert capi.device_status(clear=False) == 0
+
+
+def test_dependent_back_to_back_launches_on_shared_buffers(capi, oracle_mod):
+    """The quantizer starts early (programmatic dependent launch) and prefetches
+    X into L2 before waiting for the previous kernel.  Here every step first
+    overwrites X in place with another kernel, then quantizes it into the same
+    Q/S buffers, then copies Q/S out: each result must match its own input."""
+    m, k = 2048, 4096
+    srcs = [inputs.normal(m, k, 300 + i, sigma=float(i + 1)) for i in range(4)]
+    dev = [torch.from_numpy(b.view(np.int16)).cuda() for b in srcs]
+    expect = [oracle_mod.quantize(b, "bf16", m, k) for b in srcs]
+    sb = capi.scale_storage_bytes(m, k)
+    x = torch.empty_like(dev[0])
+    q = torch.empty((m, k), dtype=torch.uint8, device="cuda")
+    s = torch.empty((sb,), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for step in range(24):
+        x.copy_(dev[step % 4])
+        capi.quantize(x.data_ptr(), 0, m, k, k, q.data_ptr(), m, k, k, s.data_ptr(), sb, st)
+        if step % 3 == 2:  # also chain quantizer -> quantizer on the same buffers
+            capi.quantize(x.data_ptr(), 0, m, k, k, q.data_ptr(), m, k, k, s.data_ptr(), sb, st)
+        outs.append((q.clone(), s.clone()))
+    torch.cuda.synchronize()
+    for step, (qq, ss) in enumerate(outs):
+        q_ref, s_ref = expect[step % 4]
+        assert np.array_equal(qq.cpu().numpy(), q_ref), step
+        assert np.array_equal(ss.cpu().numpy(), s_ref), step
