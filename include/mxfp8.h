@@ -125,11 +125,19 @@ MXFP8_API int mxfp8_dequantize(const void* q, int64_t rows, int64_t cols, int64_
 /* Sticky device-side error word of the current device (0 = none).  Kernels
  * never trap: a pipeline wait that exceeds its time limit (about 1 s) sets a
  * bit here and the kernel returns early.  Bits: 1 = payload tile wait,
- * 2 = stage-release wait, 4 = drain wait on exit.  Reading synchronises the
+ * 2 = stage-release wait, 4 = drain wait on exit, 8 = the self-test's wait.  Reading synchronises the
  * device; clear != 0 resets the word.  The word lives in a small device
  * buffer allocated on the first quantize call on each device.
  * No counterpart in the reference (its kernel waits without a limit). */
 MXFP8_API int mxfp8_device_status(uint32_t* status_out, int clear);
+
+/* Failure-path self-test: launches one CTA that waits, with the same bounded
+ * wait the quantizer pipeline uses, on an mbarrier nothing completes; after
+ * limit_us (1 .. 10^7) it gives up, sets bit 8 of the device status word and
+ * returns.  No fault, no trap: the context stays usable.  Read the result
+ * with mxfp8_device_status after synchronising.
+ * No counterpart in the reference (its kernel waits without a limit). */
+MXFP8_API int mxfp8_selftest_bounded_wait(uint32_t limit_us, mxfp8_stream_t stream);
 
 /* Name of a status code. */
 MXFP8_API const char* mxfp8_strerror(int status);

@@ -37,6 +37,7 @@ EXPORTS = (
     "mxfp8_quantize_padded",
     "mxfp8_dequantize",
     "mxfp8_device_status",
+    "mxfp8_selftest_bounded_wait",
     "mxfp8_strerror",
     "mxfp8_last_error",
 )
@@ -76,6 +77,8 @@ def lib() -> ctypes.CDLL:
         L.mxfp8_dequantize.restype = i32
         L.mxfp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]
         L.mxfp8_device_status.restype = i32
+        L.mxfp8_selftest_bounded_wait.argtypes = [ctypes.c_uint32, vp]
+        L.mxfp8_selftest_bounded_wait.restype = i32
         L.mxfp8_strerror.argtypes = [i32]
         L.mxfp8_strerror.restype = ctypes.c_char_p
         L.mxfp8_last_error.argtypes = []
@@ -147,3 +150,8 @@ def device_status(clear: bool = False) -> int:
     v = ctypes.c_uint32(0)
     check(lib().mxfp8_device_status(ctypes.byref(v), int(clear)), "device status read")
     return int(v.value)
+
+
+def selftest_bounded_wait(limit_us: int, stream: int) -> None:
+    """Launch the bounded-wait self-test kernel (see include/mxfp8.h)."""
+    check(lib().mxfp8_selftest_bounded_wait(limit_us, stream or None), "bounded-wait self-test launch")

@@ -19,7 +19,7 @@ PKG = pathlib.Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libmxfp8.so"
-SOURCES = ["capi.cu", "quantize_tma.cu", "quantize_generic.cu", "dequantize.cu"]
+SOURCES = ["capi.cu", "quantize_tma.cu", "quantize_generic.cu", "dequantize.cu", "selftest.cu"]
 HEADERS = ["ptx.cuh", "recipe.cuh", "launch.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

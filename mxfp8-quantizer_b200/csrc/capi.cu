@@ -232,6 +232,14 @@ extern "C" MXFP8_API int mxfp8_device_status(uint32_t* status_out, int clear) {
     return MXFP8_OK;
 }
 
+extern "C" MXFP8_API int mxfp8_selftest_bounded_wait(uint32_t limit_us, mxfp8_stream_t stream) {
+    if (limit_us == 0 || limit_us > 10000000u) return MXFP8_ERR_SHAPE;
+    DeviceState* dev = nullptr;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    return launch_bounded_wait_selftest(dev->status, limit_us, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" MXFP8_API const char* mxfp8_strerror(int status) {
     switch (status) {
         case MXFP8_OK: return "success";

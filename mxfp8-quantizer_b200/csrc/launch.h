@@ -28,6 +28,8 @@ int launch_quantize_tma_noalloc(const QuantizeArgs& a, int dev, int sm_count, cu
 int launch_dequantize(const uint8_t* q, int64_t rows, int64_t cols, int64_t ld_q, const uint8_t* s,
                       void* out, int out_dtype, int64_t ld_out, cudaStream_t stream);
 
+int launch_bounded_wait_selftest(unsigned int* status, uint32_t limit_us, cudaStream_t stream);
+
 // Records the CUDA error text for mxfp8_last_error() on this host thread.
 void set_last_error(const char* what, int code);
 

@@ -289,3 +289,41 @@ def test_dependent_back_to_back_launches_on_shared_buffers(capi, oracle_mod):
         q_ref, s_ref = expect[step % 4]
         assert np.array_equal(qq.cpu().numpy(), q_ref), step
         assert np.array_equal(ss.cpu().numpy(), s_ref), step
+
+
+def test_bounded_wait_times_out_and_reports(capi, golden):
+    """Failure path without a GPU fault: an mbarrier wait that nothing
+    completes gives up after its limit, sets the status bit, and the context
+    keeps working (a quantization right after is still bit-exact)."""
+    import time
+
+    assert capi.device_status(clear=True) == 0
+    t0 = time.perf_counter()
+    capi.selftest_bounded_wait(50_000, torch.cuda.current_stream().cuda_stream)  # 50 ms
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert capi.device_status(clear=True) == 8
+    assert 0.04 < elapsed < 5.0
+    assert capi.device_status(clear=False) == 0
+    q, s = gpu_quantize(capi, inputs.normal(256, 1024, 0), "bf16", 256, 1024)   # config 1
+    assert sha(q) == golden["cases"]["c1"]["q_sha256"] and sha(s) == golden["cases"]["c1"]["s_sha256"]
+
+
+def test_host_quantizer_matches_device_path(capi, oracle_mod):
+    """HostQuantizer (pinned host X in, host Q/S out, row chunks over three
+    streams) gives the bytes of the device path, for a ragged row count."""
+    import MXFP8_quantizer
+
+    pkg = MXFP8_quantizer.load_package()
+    m, k = 2500, 1000
+    bits = inputs.normal(m, k, 55, "fp16", sigma=4.0)
+    x_host = inputs.bits_to_torch(bits, "fp16").pin_memory()
+    hq = pkg.HostQuantizer(m, k, torch.float16, chunk_rows=512)
+    q_host = torch.empty((m, hq.q_cols), dtype=torch.uint8).pin_memory()
+    s_host = torch.empty((hq.s_bytes,), dtype=torch.uint8).pin_memory()
+    for _ in range(2):
+        hq(x_host, q_host, s_host)
+    torch.cuda.synchronize()
+    q_ref, s_ref = oracle_mod.quantize(bits, "fp16", m, hq.q_cols)
+    assert np.array_equal(q_host.numpy(), q_ref)
+    assert np.array_equal(s_host.numpy(), s_ref)
