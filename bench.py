@@ -246,6 +246,61 @@ def sys_path_oracle():
         sys.path.insert(0, p)
 
 
+def dequantize_arm(args, pkg, capi, xs, qs, ss, launch, n_ws, m, k, s_bytes, stream, barrier, max_over_ranks,
+                   rank, world, l2, ws_bytes) -> None:
+    """Time mxfp8_dequantize (E4M3 payload + packed scales -> bf16) on this
+    rank's workload: reads MK + MK/32 bytes, writes 2MK."""
+    import torch
+
+    for i in range(n_ws):
+        launch(i)
+    ys = [torch.empty((m, k), dtype=torch.bfloat16, device=xs[0].device) for _ in range(n_ws)]
+    lib = capi.lib()
+    sh = stream.cuda_stream
+    args_d = [(qs[i].data_ptr(), m, k, k, ss[i].data_ptr(), ys[i].data_ptr(), capi.BF16, k, sh) for i in range(n_ws)]
+
+    def deq(i):
+        rc = lib.mxfp8_dequantize(*args_d[i])
+        if rc:
+            capi.check(rc, "bench dequantize")
+
+    deq(0)
+    torch.cuda.synchronize()
+    # dequantize(quantize(x)) differs from x by at most one E4M3 rounding step per element
+    err = (ys[0].float() - xs[0].float()).abs()
+    bound = xs[0].float().abs() * 2.0 ** -4 + 2.0 ** -120
+    if not bool((err <= bound).all()):
+        raise SystemExit("dequantize round trip out of bounds")
+    for i in range(args.warmup):
+        deq(i % n_ws)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(args.steps):
+        deq(i % n_ws)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    elapsed = start.elapsed_time(end)
+    max_ms = max_over_ranks(elapsed)
+    nbytes = m * k + s_bytes + 2 * m * k
+    peak, peak_kind = measured_hbm_peak()
+    achieved = nbytes / (elapsed / args.steps * 1e-3) / 1e9
+    if rank == 0:
+        line = base_line(args, world)
+        line["metric"] = "effective TB/s of mxfp8_dequantize (MK + MK/32 read + 2MK bf16 write) / device time"
+        line["config"]["workload"] = f"{m}x{k} e4m3 + ue8m0 -> bf16 per rank"
+        line["config"]["l2"] = f"{n_ws} rotating workspaces"
+        line.update({"op": "dequantize", "value": world * nbytes / (max_ms / args.steps * 1e-3) / 1e12,
+                     "ms_per_step": max_ms / args.steps,
+                     "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                                  "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                                  "algorithmic_bytes_per_launch": nbytes},
+                     "gpu_launches": args.steps})
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -258,6 +313,8 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=K_DEFAULT)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=["quantize", "dequantize"], default="quantize",
+                    help="dequantize: time mxfp8_dequantize (E4M3 + scales -> bf16) on the same workload")
     ap.add_argument("--profile", action="store_true",
                     help="kernel launches only (verify, warm-up, K launches): the command profiled with ncu")
     args = ap.parse_args()
@@ -314,6 +371,13 @@ def main() -> None:
         rc = lib.mxfp8_quantize(*launch_args[i])
         if rc:
             capi.check(rc, "bench launch")
+
+    if args.op == "dequantize":
+        dequantize_arm(args, pkg, capi, xs, qs, ss, launch, n_ws, m, k, s_bytes, stream, barrier, max_over_ranks,
+                       rank, world, l2, ws_bytes)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     # correctness gate before timing (the reference does the same, MXFP8_quantizer.py:912-935)
     launch(0)

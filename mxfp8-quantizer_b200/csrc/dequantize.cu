@@ -3,6 +3,11 @@
 // reference's end-to-end check applies on the host
 // (MXFP8_quantizer.py:1179-1187); here it is one streaming kernel.  Scale
 // byte 255 is the UE8M0 NaN; byte 0 is 2^-127.
+//
+// Thread map: one thread per 16 payload bytes (half a scale block), so a
+// warp reads 512 contiguous payload bytes with 16-byte loads and writes
+// 1-2 KiB contiguous output with 16-byte stores.  Falls back to byte loads
+// and element stores when a row is not 16-byte aligned.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -25,58 +30,87 @@ __device__ __forceinline__ float ue8m0_to_float(uint32_t b) {
     return __uint_as_float(b << 23);
 }
 
+// 16 decoded values -> out (16 contiguous elements at element index o).
 template <int OUT>
-__device__ __forceinline__ void store_out(void* out, int64_t idx, float v) {
+__device__ __forceinline__ void store16(void* out, int64_t o, const float (&v)[16], bool vec) {
     if constexpr (OUT == MXFP8_F32) {
-        static_cast<float*>(out)[idx] = v;
-    } else if constexpr (OUT == MXFP8_BF16) {
-        static_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
+        float* p = static_cast<float*>(out) + o;
+        if (vec) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                __stcs(reinterpret_cast<float4*>(p) + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) p[i] = v[i];
+        }
     } else {
-        static_cast<__half*>(out)[idx] = __float2half_rn(v);
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if constexpr (OUT == MXFP8_BF16) {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            } else {
+                const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+        }
+        uint16_t* p = static_cast<uint16_t*>(out) + o;
+        if (vec) {
+            __stcs(reinterpret_cast<uint4*>(p), make_uint4(w[0], w[1], w[2], w[3]));
+            __stcs(reinterpret_cast<uint4*>(p) + 1, make_uint4(w[4], w[5], w[6], w[7]));
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                p[2 * i] = (uint16_t)(w[i] & 0xFFFFu);
+                p[2 * i + 1] = (uint16_t)(w[i] >> 16);
+            }
+        }
     }
 }
 
-// One thread per (row, 32-element block).
 template <int OUT>
 __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restrict__ q, int64_t rows, int64_t cols,
                                                          int64_t ld_q, const uint8_t* __restrict__ s, void* out,
                                                          int64_t ld_out) {
-    const int64_t nblk = cols / 32;
-    const int64_t col_chunks = (nblk + 3) / 4;
-    const int64_t n = rows * nblk;
+    const int64_t halves = cols / 16;                 // 16-byte payload pieces per row
+    const int64_t col_chunks = (cols / 32 + 3) / 4;
+    const int64_t n = rows * halves;
+    constexpr int kOutBytes = OUT == MXFP8_F32 ? 4 : 2;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
          idx += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = idx / nblk;
-        const int64_t b = idx - r * nblk;
-        const float scale = ue8m0_to_float(s[scale_offset(r, b, col_chunks)]);
-        const uint8_t* src = q + r * ld_q + b * 32;
-        uint32_t w[8];
+        const int64_t r = idx / halves;
+        const int64_t hp = idx - r * halves;
+        const float scale = ue8m0_to_float(__ldg(s + scale_offset(r, hp >> 1, col_chunks)));
+        const uint8_t* src = q + r * ld_q + hp * 16;
+        uint32_t w[4];
         if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-            const uint4 a = reinterpret_cast<const uint4*>(src)[0];
-            const uint4 c = reinterpret_cast<const uint4*>(src)[1];
+            const uint4 a = __ldcs(reinterpret_cast<const uint4*>(src));
             w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-            w[4] = c.x; w[5] = c.y; w[6] = c.z; w[7] = c.w;
         } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < 4; ++i)
                 w[i] = src[4 * i] | (src[4 * i + 1] << 8) | (src[4 * i + 2] << 16) | ((uint32_t)src[4 * i + 3] << 24);
         }
-        const int64_t o = r * ld_out + b * 32;
+        float v[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
             const float2 lo = e4m3x2_to_float2(w[i] & 0xFFFFu);
             const float2 hi = e4m3x2_to_float2(w[i] >> 16);
-            store_out<OUT>(out, o + 4 * i + 0, __fmul_rn(lo.x, scale));
-            store_out<OUT>(out, o + 4 * i + 1, __fmul_rn(lo.y, scale));
-            store_out<OUT>(out, o + 4 * i + 2, __fmul_rn(hi.x, scale));
-            store_out<OUT>(out, o + 4 * i + 3, __fmul_rn(hi.y, scale));
+            v[4 * i + 0] = __fmul_rn(lo.x, scale);
+            v[4 * i + 1] = __fmul_rn(lo.y, scale);
+            v[4 * i + 2] = __fmul_rn(hi.x, scale);
+            v[4 * i + 3] = __fmul_rn(hi.y, scale);
         }
+        const int64_t o = r * ld_out + hp * 16;
+        const bool vec = ((reinterpret_cast<uintptr_t>(out) + (uint64_t)o * kOutBytes) & 15) == 0;
+        store16<OUT>(out, o, v, vec);
     }
 }
 
 int launch_dequantize(const uint8_t* q, int64_t rows, int64_t cols, int64_t ld_q, const uint8_t* s, void* out,
                       int out_dtype, int64_t ld_out, cudaStream_t stream) {
-    const int64_t n = rows * (cols / 32);
+    const int64_t n = rows * (cols / 16);
     if (n == 0) return MXFP8_OK;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

@@ -38,6 +38,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/mxfp8.h"
@@ -312,8 +313,16 @@ template <int DT>
 static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
     using L = Layout<kStages>;
     auto kernel = quantize_tma_kernel<DT, kStages>;
-    // The attribute is per device; set it on every launch path (cheap).
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::alloc);
+    // The shared-memory opt-in is per device: set it once per device, so that
+    // later launches (including ones under stream capture) make no such call.
+    static std::atomic<uint64_t> attr_set{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (e == cudaSuccess && !(attr_set.load(std::memory_order_acquire) & bit)) {
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::alloc);
+        if (e == cudaSuccess) attr_set.fetch_or(bit, std::memory_order_acq_rel);
+    }
     if (e != cudaSuccess) {
         set_last_error("cudaFuncSetAttribute", (int)e);
         return MXFP8_ERR_CUDA;

@@ -327,3 +327,56 @@ def test_host_quantizer_matches_device_path(capi, oracle_mod):
     q_ref, s_ref = oracle_mod.quantize(bits, "fp16", m, hq.q_cols)
     assert np.array_equal(q_host.numpy(), q_ref)
     assert np.array_equal(s_host.numpy(), s_ref)
+
+
+def test_dequantize_unaligned_output_rows(capi, oracle_mod):
+    """Output rows that are not 16-byte aligned take the element-store path."""
+    m, k = 64, 96
+    bits = inputs.normal(m, k, 17, sigma=5.0)
+    q_ref, s_ref = oracle_mod.quantize(bits, "bf16", m, k)
+    q = torch.from_numpy(q_ref).cuda()
+    s = torch.from_numpy(s_ref).cuda()
+    ld = k + 1
+    out = torch.full((m * ld + 8,), float("nan"), dtype=torch.float32, device="cuda")
+    capi.dequantize(q.data_ptr(), m, k, k, s.data_ptr(), out.data_ptr() + 4, capi.F32, ld,
+                    torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = out[1:1 + m * ld].view(m, ld)[:, :k].cpu().numpy()
+    np.testing.assert_array_equal(got, oracle_mod.dequantize(q_ref, s_ref))
+
+
+def test_quantize_inside_cuda_graph(capi, oracle_mod):
+    """Launches captured in a CUDA graph (dependent-launch edges between them)
+    replay bit-exactly; inputs are refreshed in place between replays."""
+    m, k = 1024, 2048
+    srcs = [inputs.normal(m, k, 700 + i) for i in range(3)]
+    sb = capi.scale_storage_bytes(m, k)
+    x = torch.empty((m, k), dtype=torch.int16, device="cuda")
+    q = torch.empty((3, m, k), dtype=torch.uint8, device="cuda")
+    s = torch.empty((3, sb), dtype=torch.uint8, device="cuda")
+    x.copy_(torch.from_numpy(srcs[0].view(np.int16)))
+    capi.quantize(x.data_ptr(), 0, m, k, k, q[0].data_ptr(), m, k, k, s[0].data_ptr(), sb,
+                  torch.cuda.current_stream().cuda_stream)      # first call outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st = torch.cuda.current_stream().cuda_stream
+        for i in range(3):
+            capi.quantize(x.data_ptr(), 0, m, k, k, q[i].data_ptr(), m, k, k, s[i].data_ptr(), sb, st)
+    for src in srcs:
+        x.copy_(torch.from_numpy(src.view(np.int16)))
+        g.replay()
+        torch.cuda.synchronize()
+        q_ref, s_ref = oracle_mod.quantize(src, "bf16", m, k)
+        for i in range(3):
+            assert np.array_equal(q[i].cpu().numpy(), q_ref)
+            assert np.array_equal(s[i].cpu().numpy(), s_ref)
+    del g
+
+
+def test_e2e_suite_all_configs(capi):
+    import MXFP8_quantizer
+
+    r = MXFP8_quantizer.run_e2e_suite()
+    assert r["e2e_suite_passed"] and r["num_configs"] == 6
+    assert all(c["quantizer_verify_passed"] and c["max_err_ratio"] < 1.0 for c in r["configs"])
