@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int qb = it % kQBufs;
             const int rt = t / p.n_col_tiles;
             const int ct = t - rt * p.n_col_tiles;
-            // warp-uniform verdict, so the __syncwarp below is never divergent
+            // warp-uniform outcome, so the __syncwarp below is never divergent
             const bool ok =
                 __all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, (it / STAGES) & 1, kWaitLimitNs));
             if (ok) {
