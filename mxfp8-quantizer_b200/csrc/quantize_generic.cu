@@ -1,7 +1,17 @@
-// quantize_generic.cu -- plain-load MXFP8 quantizer for layouts the TMA path
-// cannot describe (X or Q not 16-byte aligned, row strides that are not
-// multiples of 16 bytes, empty X).  Same recipe and output contract as the
-// TMA kernel; one thread per (row, 4-block scale word).
+// quantize_generic.cu -- MXFP8 quantizer for layouts the TMA path cannot
+// describe: X rows that are not 16-byte aligned (odd K, row strides that are
+// not multiples of 8 elements, 2-byte aligned views), Q rows that are not
+// 16-byte aligned, empty X.  Same recipe (recipe.cuh) and output contract.
+//
+// Work item: 4 rows x one 256-column segment (8 scale blocks), one warp.
+// Lane l owns columns [8l, 8l + 8) of the segment, so a quad of lanes holds
+// one 1x32 block (amax via two xor-shuffles, as in the reference kernel,
+// MXFP8_quantizer.py:157-168).  Loads are 4-byte words: a row whose first
+// element is 4-byte aligned takes 4 words per lane; a row that starts 2 bytes
+// past a word boundary takes the 5 aligned words around its 8 elements and
+// re-aligns them with a byte permute.  A word is loaded only if it holds an
+// element of the row, and an aligned 4-byte word never crosses a page, so no
+// load touches memory outside X's pages; elements outside (m, k) are zeroed.
 #include <cuda_runtime.h>
 
 #include "../../include/mxfp8.h"
@@ -10,66 +20,114 @@
 
 namespace mxfp8 {
 
+constexpr int kRowsPerItem = 4;
+
+// Eight elements of row `row` starting at column c (c % 8 == 0), zero outside
+// [0, k), as four words of two packed elements.
+__device__ __forceinline__ void load8(const uint16_t* row, int64_t c, int64_t k, uint32_t (&w)[4]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(row + c);
+    if ((a & 3u) == 0) {
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(a);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = (c + 2 * j < k) ? __ldg(p + j) : 0u;
+    } else {
+        // element c sits in the upper half of the word at a - 2
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(a - 2);
+        uint32_t v[5];
+#pragma unroll
+        for (int j = 0; j < 5; ++j) v[j] = (c + 2 * j - 1 < k) ? __ldg(p + j) : 0u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = __byte_perm(v[j], v[j + 1], 0x5432);
+    }
+    // zero the columns at and beyond k (the loaded words may carry neighbours)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (c + 2 * j >= k) w[j] = 0u;
+        else if (c + 2 * j + 1 >= k) w[j] &= 0xFFFFu;
+    }
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t quad_quantize(const uint32_t (&w)[4], uint2& q) {
+    uint32_t m = __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu), __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+    m = max(m & 0xFFFFu, m >> 16);
+    m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+    uint32_t byte;
+    float inv;
+    scale_from_amax<DT>(m, byte, inv);
+    q.x = quantize_pair<DT>(w[0], inv) | (quantize_pair<DT>(w[1], inv) << 16);
+    q.y = quantize_pair<DT>(w[2], inv) | (quantize_pair<DT>(w[3], inv) << 16);
+    return byte;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(256) quantize_generic_kernel(const uint16_t* __restrict__ x, int64_t m, int64_t k,
                                                                int64_t ld_x, uint8_t* __restrict__ q,
                                                                int64_t q_rows, int64_t q_cols, int64_t ld_q,
                                                                uint8_t* __restrict__ s, int64_t scale_rows,
                                                                int64_t scale_cols, int64_t col_chunks) {
-    const int64_t n = scale_rows * col_chunks;
-    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = idx / col_chunks;
-        const int64_t cc = idx - r * col_chunks;
-        uint32_t word = 0;
-        if (r < q_rows) {
-#pragma unroll 1
-            for (int bi = 0; bi < 4; ++bi) {
-                const int64_t blk = cc * 4 + bi;
-                if (blk >= scale_cols) break;
-                const int64_t c0 = blk * 32;
-                uint32_t w[16];
+    const int lane = threadIdx.x & 31;
+    const int64_t segs = (col_chunks + 1) / 2;               // 256-column segments
+    const int64_t groups = (scale_rows + kRowsPerItem - 1) / kRowsPerItem;
+    const int64_t items = segs * groups;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t it = warp0; it < items; it += nwarps) {
+        const int64_t g = it / segs;
+        const int64_t seg = it - g * segs;
+        const int64_t c = seg * 256 + lane * 8;
+        uint32_t w[kRowsPerItem][4];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int64_t c = c0 + 2 * e;
-                    uint32_t lo = 0, hi = 0;
-                    if (r < m) {
-                        if (c < k) lo = __ldg(x + r * ld_x + c);
-                        if (c + 1 < k) hi = __ldg(x + r * ld_x + c + 1);
-                    }
-                    w[e] = lo | (hi << 16);
-                }
-                uint32_t qw[8];
-                const uint32_t byte = quantize_block<DT>(w, qw);
-                uint8_t* dst = q + r * ld_q + c0;
-                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                    reinterpret_cast<uint4*>(dst)[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
-                    reinterpret_cast<uint4*>(dst)[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) dst[e] = (uint8_t)(qw[e >> 2] >> (8 * (e & 3)));
-                }
-                word |= byte << (8 * bi);
+        for (int u = 0; u < kRowsPerItem; ++u) {
+            const int64_t r = g * kRowsPerItem + u;
+            if (r < m && c < k) {
+                load8(x + r * ld_x, c, k, w[u]);
+            } else {
+                w[u][0] = w[u][1] = w[u][2] = w[u][3] = 0u;
             }
         }
-        // the four scale bytes of (r, 4*cc .. 4*cc+3) are one aligned word
-        *reinterpret_cast<uint32_t*>(s + scale_offset(r, cc * 4, col_chunks)) = word;
+#pragma unroll
+        for (int u = 0; u < kRowsPerItem; ++u) {
+            const int64_t r = g * kRowsPerItem + u;
+            if (r >= scale_rows) break;                       // warp-uniform
+            uint2 qq;
+            uint32_t byte = quad_quantize<DT>(w[u], qq);
+            if (r < q_rows && c < q_cols) {
+                uint8_t* dst = q + r * ld_q + c;
+                if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+                    *reinterpret_cast<uint2*>(dst) = qq;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) dst[e] = (uint8_t)((e < 4 ? qq.x : qq.y) >> (8 * (e & 3)));
+                }
+            }
+            const int64_t blk = seg * 8 + (lane >> 2);
+            if (r >= q_rows || blk >= scale_cols) byte = 0;
+            // quads 0-3 -> lane 0, quads 4-7 -> lane 16: one packed word each
+            const uint32_t b1 = __shfl_down_sync(0xFFFFFFFFu, byte, 4);
+            const uint32_t b2 = __shfl_down_sync(0xFFFFFFFFu, byte, 8);
+            const uint32_t b3 = __shfl_down_sync(0xFFFFFFFFu, byte, 12);
+            if ((lane & 15) == 0 && (blk >> 2) < col_chunks)
+                *reinterpret_cast<uint32_t*>(s + scale_offset(r, blk, col_chunks)) =
+                    byte | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
     }
 }
 
 int launch_quantize_generic(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
-    const int64_t n = a.scale_rows * a.col_chunks;
-    const int threads = 256;
-    int64_t blocks = (n + threads - 1) / threads;
+    const int64_t segs = (a.col_chunks + 1) / 2;
+    const int64_t items = segs * ((a.scale_rows + kRowsPerItem - 1) / kRowsPerItem);
+    int64_t blocks = (items * 32 + 255) / 256;
     const int64_t cap = (int64_t)sm_count * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     const uint16_t* x = static_cast<const uint16_t*>(a.x);
     if (a.dtype == kBF16)
-        quantize_generic_kernel<kBF16><<<(int)blocks, threads, 0, stream>>>(
+        quantize_generic_kernel<kBF16><<<(int)blocks, 256, 0, stream>>>(
             x, a.m, a.k, a.ld_x, a.q, a.q_rows, a.q_cols, a.ld_q, a.s, a.scale_rows, a.scale_cols, a.col_chunks);
     else
-        quantize_generic_kernel<kFP16><<<(int)blocks, threads, 0, stream>>>(
+        quantize_generic_kernel<kFP16><<<(int)blocks, 256, 0, stream>>>(
             x, a.m, a.k, a.ld_x, a.q, a.q_rows, a.q_cols, a.ld_q, a.s, a.scale_rows, a.scale_cols, a.col_chunks);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

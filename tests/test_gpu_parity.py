@@ -380,3 +380,15 @@ def test_e2e_suite_all_configs(capi):
     r = MXFP8_quantizer.run_e2e_suite()
     assert r["e2e_suite_passed"] and r["num_configs"] == 6
     assert all(c["quantizer_verify_passed"] and c["max_err_ratio"] < 1.0 for c in r["configs"])
+
+
+@pytest.mark.parametrize("m,k,x_offset,dtype", [(1000, 4097, 0, "bf16"), (333, 4064, 1, "bf16"), (129, 8191, 3, "fp16"),
+                                                (64, 31, 1, "fp16"), (1, 1, 1, "bf16"), (260, 300, 0, "bf16")])
+def test_plain_load_path_odd_layouts_special_values(m, k, x_offset, dtype, capi, oracle_mod):
+    """Odd K and 2-byte aligned X go through the plain-load kernel; special
+    values, both geometries."""
+    kk = (k + 31) // 32 * 32
+    bits = inputs.special_values_bf16(m, kk, seed=k)[:, :k].copy() if dtype == "bf16" else \
+        inputs.normal(m, k, k, "fp16", sigma=30.0)
+    check_against_oracle(capi, oracle_mod, bits, dtype, x_offset=x_offset)
+    check_against_oracle(capi, oracle_mod, bits, dtype, m, kk, x_offset=x_offset)
