@@ -392,3 +392,33 @@ def test_plain_load_path_odd_layouts_special_values(m, k, x_offset, dtype, capi,
         inputs.normal(m, k, k, "fp16", sigma=30.0)
     check_against_oracle(capi, oracle_mod, bits, dtype, x_offset=x_offset)
     check_against_oracle(capi, oracle_mod, bits, dtype, m, kk, x_offset=x_offset)
+
+
+def test_randomized_shapes_layouts_and_values(capi, oracle_mod):
+    """40 seeded random cases: shape, dtype, geometry, row stride, base offset
+    and value distribution (normal, log-uniform with specials, subnormal-heavy)."""
+    rng = np.random.default_rng(2024)
+    for case in range(40):
+        m = int(rng.integers(1, 400))
+        k = int(rng.integers(1, 1500))
+        dtype = "bf16" if rng.random() < 0.6 else "fp16"
+        kind = rng.integers(0, 3)
+        if kind == 0:
+            bits = inputs.normal(m, k, case, dtype, sigma=float(10 ** rng.uniform(-3, 3)))
+        elif kind == 1 and dtype == "bf16":
+            kk = (k + 31) // 32 * 32
+            bits = inputs.special_values_bf16(m, kk, seed=case)[:, :k].copy()
+        else:
+            bits = inputs.normal(m, k, case, dtype)
+            sub = rng.random((m, k)) < 0.3
+            bits[sub] = rng.integers(0, 0x80 if dtype == "bf16" else 0x400, size=int(sub.sum())).astype(np.uint16)
+        kw = {}
+        r = rng.random()
+        if r < 0.2:
+            kw["ld_x"] = k + int(rng.integers(1, 40))
+        elif r < 0.35:
+            kw["x_offset"] = int(rng.integers(1, 8))
+        if rng.random() < 0.5:
+            check_against_oracle(capi, oracle_mod, bits, dtype, **kw)
+        else:
+            check_against_oracle(capi, oracle_mod, bits, dtype, m, (k + 31) // 32 * 32, **kw)
