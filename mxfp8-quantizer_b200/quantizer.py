@@ -182,8 +182,13 @@ def quantize(x: torch.Tensor, q: torch.Tensor | None = None, s: torch.Tensor | N
         q = torch.empty((q_rows, q_cols), dtype=torch.float8_e4m3fn, device=x.device)
     if s is None:
         s = torch.empty((_capi.scale_storage_bytes(q_rows, q_cols),), dtype=torch.uint8, device=x.device)
-    if q.dim() != 2 or q.shape[0] < q_rows or q.stride(1) != 1:
-        raise ValueError("q must be a row-major (q_rows, >= q_cols) byte matrix")
+    if not x.is_cuda:
+        raise ValueError("x must be a CUDA tensor")
+    if (q.dim() != 2 or q.element_size() != 1 or q.shape[0] < q_rows or q.shape[1] < q_cols
+            or q.stride(1) != 1 or q.device != x.device):
+        raise ValueError("q must be a row-major (>= q_rows, >= q_cols) one-byte matrix on x's device")
+    if s.device != x.device or not s.is_contiguous():
+        raise ValueError("s must be a contiguous buffer on x's device")
     with torch.cuda.device(x.device):
         _capi.quantize(x.data_ptr(), _dtype_code(x.dtype), m, k, x.stride(0), q.data_ptr(), q_rows, q_cols,
                        q.stride(0), s.data_ptr(), s.numel() * s.element_size(), _stream_handle(stream))
@@ -192,8 +197,13 @@ def quantize(x: torch.Tensor, q: torch.Tensor | None = None, s: torch.Tensor | N
 
 def dequantize(q: torch.Tensor, s: torch.Tensor, out_dtype: torch.dtype = torch.float32, stream=None):
     """E4M3 payload + packed UE8M0 scales -> out_dtype (bf16, fp16 or fp32)."""
+    if q.dim() != 2 or q.element_size() != 1 or q.stride(1) != 1 or not q.is_cuda:
+        raise ValueError("q must be a row-major one-byte CUDA matrix")
     rows, cols = q.shape
-    code = {torch.float32: _capi.F32, torch.bfloat16: _capi.BF16, torch.float16: _capi.FP16}[out_dtype]
+    codes = {torch.float32: _capi.F32, torch.bfloat16: _capi.BF16, torch.float16: _capi.FP16}
+    if out_dtype not in codes:
+        raise ValueError("out_dtype must be torch.float32, torch.bfloat16 or torch.float16")
+    code = codes[out_dtype]
     out = torch.empty((rows, cols), dtype=out_dtype, device=q.device)
     with torch.cuda.device(q.device):
         _capi.dequantize(q.data_ptr(), rows, cols, q.stride(0), s.data_ptr(), out.data_ptr(), code, out.stride(0),

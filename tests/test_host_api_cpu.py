@@ -70,3 +70,13 @@ def test_config_validation_matches_reference_rules():
         pkg.run_e2e_verification(m=1024, n=1024, k=2000)        # K not a multiple of 256
     with pytest.raises(ValueError):
         pkg.run_e2e_verification(mma_tiler_mn=(256, 128), cluster_shape_mn=(1, 1))
+
+
+def test_quantize_wrapper_rejects_bad_tensors_on_cpu():
+    x = torch.zeros((16, 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        pkg.quantize(x)                                   # not a CUDA tensor
+    with pytest.raises(ValueError):
+        pkg.dequantize(torch.zeros((4, 32), dtype=torch.uint8), torch.zeros(512, dtype=torch.uint8))
+    with pytest.raises(ValueError):
+        pkg.quantize(torch.zeros((2, 3, 4), dtype=torch.bfloat16))
