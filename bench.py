@@ -303,6 +303,78 @@ def dequantize_arm(args, pkg, capi, xs, qs, ss, launch, n_ws, m, k, s_bytes, str
         print(json.dumps(line), flush=True)
 
 
+def c5_arm(args, rank: int, world: int, local: int) -> None:
+    """X = 131072 x 16384 bf16 N(0, 2), split by 128-row
+    chunks over the ranks (strong scaling: the whole matrix is fixed).  Each
+    rank generates its rows in 1024-row blocks from per-block seeds, so the
+    data is the same for every rank count; it quantizes its shard into its
+    slice of Q and S with no collective on the data path."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import MXFP8_quantizer
+
+    pkg = MXFP8_quantizer.load_package()
+    capi = pkg._capi
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    m_total, k = 131072, 16384
+    r0, r1 = pkg.shard.row_shard(m_total, world, rank)
+    m = r1 - r0
+    x = torch.empty((m, k), dtype=torch.bfloat16, device=dev)
+    for b0 in range(r0, r1, 1024):
+        g = torch.Generator(device=dev).manual_seed(4_000_000 + b0 // 1024)
+        n = min(1024, r1 - b0)
+        x[b0 - r0:b0 - r0 + n] = (torch.randn((1024, k), generator=g, device=dev) * 2.0)[:n].to(torch.bfloat16)
+    s_bytes = capi.scale_storage_bytes(m, k)
+    q = torch.empty((m, k), dtype=torch.uint8, device=dev)
+    s = torch.empty((s_bytes,), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+    lib = capi.lib()
+    a = (x.data_ptr(), 0, m, k, k, q.data_ptr(), m, k, k, s.data_ptr(), s_bytes, st.cuda_stream)
+    rc = lib.mxfp8_quantize(*a)
+    capi.check(rc, "c5 launch")
+    torch.cuda.synchronize()
+    ver = pkg.verify_quantizer_outputs({"x": x[:1024], "q_fp8": q[:1024].view(torch.float8_e4m3fn),
+                                        "s_storage_bytes": s[:capi.scale_storage_bytes(1024, k)]},
+                                       1024, k, 1024, k)
+    if not ver["verification_passed"]:
+        raise SystemExit(f"c5 verification failed on rank {rank}")
+    steps = max(3, min(args.steps, 200))
+    for _ in range(args.warmup):
+        lib.mxfp8_quantize(*a)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(steps):
+        lib.mxfp8_quantize(*a)
+    e1.record(st)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    mine = e0.elapsed_time(e1) / steps
+    slowest = pkg.shard.max_over_ranks(mine, device=dev)
+    fastest = -pkg.shard.max_over_ranks(-mine, device=dev)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        total = algo_bytes(m_total, k)
+        print(json.dumps({
+            "metric": "effective TB/s of BASELINE config 5 (131072x16384 bf16 N(0,2), row-sharded), max over ranks",
+            "value": total / (slowest * 1e-3) / 1e12, "unit": "TB/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": slowest, "fastest_rank_ms": fastest,
+            "per_gpu_tb_s": algo_bytes(m, k) / (slowest * 1e-3) / 1e12, "higher_is_better": True,
+            "scaling": "strong", "dtype": "f32", "data": "synthetic: N(0,2) bf16 from per-1024-row-block seeds",
+            "config": {"workload": f"131072x16384 bf16, rows [{r0}, {r1}) on rank 0 of {world}",
+                       "parallelism": f"row shards of 128-row chunks x{world}, no collective"}}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -315,6 +387,9 @@ def main() -> None:
     ap.add_argument("--k", type=int, default=K_DEFAULT)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["c2", "c5"], default="c2",
+                    help="c2: 8192x8192 per rank (weak scaling, the driver's line); "
+                         "c5: the 131072x16384 N(0,2) matrix split by 128-row chunks over the ranks (strong scaling)")
     ap.add_argument("--op", choices=["quantize", "dequantize"], default="quantize",
                     help="dequantize: time mxfp8_dequantize (E4M3 + scales -> bf16) on the same workload")
     ap.add_argument("--profile", action="store_true",
@@ -330,6 +405,9 @@ def main() -> None:
         return
     if args.impl == "reference-kernel":
         reference_kernel_arm(args, rank)
+        return
+    if args.workload == "c5":
+        c5_arm(args, rank, world, local)
         return
 
     import torch
