@@ -136,9 +136,11 @@ extern "C" MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int
     if (rc) return rc;
     a.status = dev->status;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const bool tma_ok = has_x && aligned(x, 16) && ld_x % 8 == 0 && aligned(q, 16) && ld_q % 16 == 0 &&
-                        aligned(s, 16);
-    return tma_ok ? launch_quantize_tma(a, dev->sm_count, st) : launch_quantize_generic(a, dev->sm_count, st);
+    // The pipelined kernel needs 16-byte aligned Q rows and S; it reads X
+    // through a tensor map when X's rows are 16-byte aligned and through
+    // 16-byte cp.async copies of each row's aligned span otherwise.
+    const bool out_ok = has_x && aligned(q, 16) && ld_q % 16 == 0 && aligned(s, 16);
+    return out_ok ? launch_quantize_tma(a, dev->sm_count, st) : launch_quantize_generic(a, dev->sm_count, st);
 }
 
 // Allocation-free entry: the same argument checks and kernels as

@@ -146,11 +146,11 @@ def test_layouts_and_generic_path(layout, capi, oracle_mod):
     bits = inputs.normal(333, 544, 5, "fp16")
     kw = {}
     if layout == "x_ld_odd":
-        kw = dict(ld_x=547)          # row stride not a multiple of 8 -> plain-load kernel
+        kw = dict(ld_x=547)          # row stride not a multiple of 8 -> row path
     elif layout == "x_misaligned":
-        kw = dict(x_offset=1)        # 2-byte aligned only -> plain-load kernel
+        kw = dict(x_offset=1)        # 2-byte aligned only -> row path
     elif layout == "q_misaligned":
-        kw = dict(q_offset=3)
+        kw = dict(q_offset=3)        # Q not 16-byte aligned -> plain-load kernel
     elif layout == "s_word_aligned_only":
         kw = dict(s_offset=4)
     elif layout == "x_strided_tma":
@@ -384,14 +384,43 @@ def test_e2e_suite_all_configs(capi):
 
 @pytest.mark.parametrize("m,k,x_offset,dtype", [(1000, 4097, 0, "bf16"), (333, 4064, 1, "bf16"), (129, 8191, 3, "fp16"),
                                                 (64, 31, 1, "fp16"), (1, 1, 1, "bf16"), (260, 300, 0, "bf16")])
-def test_plain_load_path_odd_layouts_special_values(m, k, x_offset, dtype, capi, oracle_mod):
-    """Odd K and 2-byte aligned X go through the plain-load kernel; special
-    values, both geometries."""
+@pytest.mark.parametrize("q_offset", [0, 8])
+def test_odd_layouts_special_values(m, k, x_offset, dtype, q_offset, capi, oracle_mod):
+    """Odd K and 2-byte aligned X: with 16-byte aligned Q they go through the
+    pipelined kernel's row path, with Q 8 bytes off through the plain-load
+    kernel.  Special values, both geometries."""
     kk = (k + 31) // 32 * 32
     bits = inputs.special_values_bf16(m, kk, seed=k)[:, :k].copy() if dtype == "bf16" else \
         inputs.normal(m, k, k, "fp16", sigma=30.0)
-    check_against_oracle(capi, oracle_mod, bits, dtype, x_offset=x_offset)
-    check_against_oracle(capi, oracle_mod, bits, dtype, m, kk, x_offset=x_offset)
+    check_against_oracle(capi, oracle_mod, bits, dtype, x_offset=x_offset, q_offset=q_offset)
+    check_against_oracle(capi, oracle_mod, bits, dtype, m, kk, x_offset=x_offset, q_offset=q_offset)
+
+
+def test_three_kernels_agree_across_launch_split(capi):
+    """38000 x 8191 bf16 (622 MB): the same X through the row path (row
+    stride 8191, two launches: 296 row tiles + 1), the tensor path (row
+    stride 8192) and the plain-load kernel (Q 8 bytes off 16-byte alignment)
+    gives identical Q and S bytes, in the reference geometry."""
+    m, k = 38000, 8191
+    q_rows, q_cols = (m + 7) // 8 * 8, (k + 255) // 256 * 256
+    s_bytes = capi.scale_storage_bytes(q_rows, q_cols)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    dense = torch.empty(m, 8192, dtype=torch.bfloat16, device="cuda")
+    dense.normal_(generator=g)
+    dense[:, :k] *= torch.logspace(-3, 3, m, device="cuda").to(torch.bfloat16)[:, None]
+    packed = dense[:, :k].contiguous()
+    stream = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for x, ld, q_off in ((packed, k, 0), (dense, 8192, 0), (dense, 8192, 8)):
+        q = torch.full((q_rows * q_cols + 16,), 0xAB, dtype=torch.uint8, device="cuda")
+        s = torch.full((s_bytes,), 0xAB, dtype=torch.uint8, device="cuda")
+        capi.quantize(x.data_ptr(), 0, m, k, ld, q.data_ptr() + q_off, q_rows, q_cols, q_cols,
+                      s.data_ptr(), s_bytes, stream)
+        outs.append((q[q_off:q_off + q_rows * q_cols], s))
+    torch.cuda.synchronize()
+    for q, s in outs[1:]:
+        assert torch.equal(q, outs[0][0]) and torch.equal(s, outs[0][1])
+    assert capi.device_status(clear=True) == 0
 
 
 def test_randomized_shapes_layouts_and_values(capi, oracle_mod):
