@@ -137,8 +137,8 @@ extern "C" MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int
     a.status = dev->status;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // The pipelined kernel needs 16-byte aligned Q rows and S; it reads X
-    // through a tensor map when X's rows are 16-byte aligned and through
-    // 16-byte cp.async copies of each row's aligned span otherwise.
+    // through one tensor map when X's rows are 16-byte aligned and through
+    // one tensor map per row phase (row % 8) otherwise.
     const bool out_ok = has_x && aligned(q, 16) && ld_q % 16 == 0 && aligned(s, 16);
     return out_ok ? launch_quantize_tma(a, dev->sm_count, st) : launch_quantize_generic(a, dev->sm_count, st);
 }

@@ -66,18 +66,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// 16-byte asynchronous copy global -> shared (both addresses 16-byte
-// aligned), bypassing L1.
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-
-// Arrive on `bar` once every cp.async this thread issued so far has landed
-// (the arrival counts against the barrier's expected count).
-__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-
 // L2 prefetch of one 2-D TMA box (no shared memory, no completion).  Only a
 // hint: L2 is where every global write lands, so a later load still sees the
 // latest data even if the lines were prefetched before it was written.
@@ -86,10 +74,6 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32
                      reinterpret_cast<uint64_t>(map)),
                  "r"(x), "r"(y)
                  : "memory");
-}
-
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Programmatic dependent launch: let the next kernel in the stream start its

@@ -33,6 +33,19 @@
 // store pass reads the 8 chunks of one row per 8-lane phase, also
 // conflict-free.
 //
+// Row path (template flag ROWS): X rows that are not 16-byte aligned (odd K,
+// row strides that are not a multiple of 8 elements, 2-byte aligned views).
+// No tensor map describes such rows, but rows r = 8j + f for a fixed phase f
+// are 8 * ld_x elements = 16 * ld_x bytes apart, always a multiple of 16.  So
+// the host encodes one tensor map per phase f (at most 8): base = the address
+// of row f rounded down to 16 bytes, which puts column c of row 8j + f at
+// element c + d_f of map row j (d_f < 8), and extent k + d_f columns by the
+// rows of that phase.  A tile is then 8 TMA loads of a 136-column x 16-row box
+// (272-byte rows, no swizzle) at column ct * 128, an aligned coordinate.
+// Every byte a box reads lies in the 16-byte chunks that hold the row's own
+// elements; columns past k + d_f and rows past the phase's last are zero
+// filled.  Consumers shift their 64 elements down by d_f in registers.
+//
 // Reference behaviour restated (not its structure): MXFP8_quantizer.py:355-525.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -66,15 +79,25 @@ constexpr uint32_t kBarCompute = 1;                       // named barrier id
 
 constexpr unsigned kErrTileWait = 1u, kErrReleaseWait = 2u, kErrDrainWait = 4u;
 
-// X staging per tile: the tensor path holds two swizzled 128x64 boxes; the
-// row path holds, per row, the 16-byte aligned span around its 128 columns
-// (at most 272 bytes: 256 plus up to 14 bytes of misalignment, rounded up).
-constexpr int kRowSlot = 272;
-constexpr int kRowStageBytes = kTileRows * kRowSlot;
-// The row path is latency-bound (its compute threads also issue the copies):
-// it runs 2 CTAs per SM with 2 stages each, ~106 KiB of shared memory apiece.
+// Row path staging: per phase, a 16-row box of 136 columns (272 bytes: 128
+// columns plus up to 7 of misalignment, a multiple of 16 bytes).
+constexpr int kPhases = 8;
+constexpr int kPhaseRows = kTileRows / kPhases;           // 16 box rows per phase and tile
+constexpr int kRowBoxCols = 136;
+constexpr int kRowSlot = kRowBoxCols * 2;                 // 272
+constexpr int kPhaseBoxBytes = kPhaseRows * kRowSlot;     // 4352 (a multiple of 128)
+constexpr int kRowStageBytes = kPhases * kPhaseBoxBytes;  // 34 KiB of X per tile
+// The row path's compute warps do more work per tile (the register shift), so
+// it runs 2 CTAs per SM with 2 stages each (~105 KiB of shared memory apiece)
+// for twice the warps: 8192 x 8191 bf16 5.92 vs 5.61 TB/s with 1 CTA x 3
+// stages (1 CTA x 4 stages 5.53, x 2 stages 4.92).
 constexpr int kRowStages = 2;
 constexpr int kRowCtasPerSm = 2;
+
+template <bool ROWS>
+struct XMaps {
+    CUtensorMap map[ROWS ? kPhases : 1];
+};
 
 template <int STAGES, bool ROWS>
 struct Layout {
@@ -84,18 +107,17 @@ struct Layout {
     static constexpr int s_off = q_off + kQBufs * kQTileBytes;
     static constexpr int bar_off = s_off + kQBufs * kSChunkBytes;
     static constexpr int ctl_off = bar_off + 2 * STAGES * 8;
-    // row path: two tables of per-row source spans (8-byte address, 4-byte size)
-    static constexpr int span_off = ctl_off + 16;
-    static constexpr int bytes = span_off + (ROWS ? 2 * kTileRows * 16 : 0);
+    static constexpr int bytes = ctl_off + 16;
     static constexpr int alloc = bytes + 1024;  // slack to align the base to 1024
 };
 
 struct TmaParams {
     int rt_offset;  // first row tile of this launch (long problems are split by row tiles)
-    const uint8_t* x;  // row path only: X base, row stride and valid extent
+    const uint8_t* x;  // row path only: X base and row stride (for each row's misalignment)
     int64_t ld_x;
     int m;
     int k;
+    int n_phases;   // row path: tensor maps in use, min(m, 8)
     uint8_t* q;
     int64_t ld_q;
     int q_rows;
@@ -125,24 +147,34 @@ __device__ __forceinline__ void report(unsigned int* status, unsigned code) {
     if (status) atomicOr(status, code);
 }
 
-// Row path: the 16-byte aligned span [src, src + bytes) that covers columns
-// [c0, min(c0 + 128, k)) of row `row`; 0 bytes if the row holds none of them.
-__device__ __forceinline__ uint32_t row_span(const TmaParams& p, int row, int c0, uint64_t& src) {
-    if (row >= p.m || c0 >= p.k) return 0u;
-    const int n = p.k - c0 < kTileCols ? p.k - c0 : kTileCols;
-    const uint64_t a = reinterpret_cast<uint64_t>(p.x) + 2ull * ((uint64_t)row * p.ld_x + c0);
-    const uint64_t lo = a & ~15ull, hi = (a + 2ull * n + 15ull) & ~15ull;
-    src = lo;
-    return (uint32_t)(hi - lo);
+// Row of the tile that compute thread `tid` handles.  Tensor path: tid % 128.
+// Row path: the 8 lanes of a shared-memory phase take 8 rows of one tensor-map
+// phase (rows 8j + f, consecutive j), whose 272-byte box rows start in 8
+// different 16-byte bank groups, so the X reads stay conflict-free.
+template <bool ROWS>
+__device__ __forceinline__ int tile_row(int tid) {
+    const int t = tid & (kTileRows - 1);
+    if (!ROWS) return t;
+    const int j = (t & 7) | ((t >> 6) << 3);
+    const int f = (t >> 3) & 7;
+    return j * kPhases + f;
+}
+
+// XOR key of the payload staging buffer's 128-byte swizzle for tile row r:
+// distinct across the 8 rows that one 8-lane phase writes.
+template <bool ROWS>
+__device__ __forceinline__ uint32_t stage_key(int r) {
+    return ROWS ? (uint32_t)((r >> 3) & 7) : (uint32_t)(r & 7);
 }
 
 // Row path: this thread's 64 elements (columns c0 + 64h ..) of row `row` from
-// its staged span, re-aligned to 16-bit lanes and zeroed outside (m, k).
-// The span starts at a 16-byte boundary and column c0 sits `off` bytes into
-// it (off < 16, even).  The thread loads the 9 aligned 16-byte words from
-// byte 128h on (row slots are 17 words apart, so 8 consecutive rows hit 8
-// different bank groups: conflict-free), then shifts them down by off bytes
-// in registers: by 8 bytes, by 4 bytes, then a byte permute for 2.
+// its 272-byte box row, re-aligned to 16-bit lanes and zeroed outside (m, k).
+// Column c0 sits `off` bytes into the box row (off < 16, even).  The thread
+// loads the 9 aligned 16-byte words from byte 128h on (conflict-free, see
+// tile_row), then shifts them down by off bytes in registers: by 8 bytes, by
+// 4 bytes, then a byte permute.  4-byte loads from byte off & ~3 instead save
+// the selects but conflict whenever the rows of a warp share their word
+// offset (2-byte aligned views with ld_x % 8 == 0: 5.46 vs 6.02 TB/s).
 __device__ __forceinline__ void read_row_words(const TmaParams& p, const uint8_t* slot, int row, int c0, int h,
                                                uint32_t (&w0)[16], uint32_t (&w1)[16]) {
     const int cf = c0 + 64 * h;
@@ -185,64 +217,34 @@ __device__ __forceinline__ void read_row_words(const TmaParams& p, const uint8_t
     }
 }
 
-// Row path: threads 0-127 each write one row's span of tile t (source
-// address, byte count) into a 128-entry table in shared memory, so that the
-// copies below read two words per chunk instead of recomputing the span.
-// A barrier among the compute threads separates the writes from the copies.
-__device__ __forceinline__ void write_row_span(const TmaParams& p, uint8_t* table, int t, int tid) {
-    if (tid >= kTileRows) return;
-    const int rt_local = t / p.n_col_tiles;
-    const int ct = t - rt_local * p.n_col_tiles;
-    uint64_t src = 0;
-    const uint32_t bytes = row_span(p, (rt_local + p.rt_offset) * kTileRows + tid, ct * kTileCols, src);
-    *reinterpret_cast<uint4*>(table + tid * 16) = make_uint4((uint32_t)src, (uint32_t)(src >> 32), bytes, 0u);
-}
-
-// Row path: this compute thread's share of a tile's copies into `stage`
-// (spans from `table`), then one arrival on the stage barrier when they have
-// landed.  The tile's 128 rows x 17 chunks of 16 bytes are numbered row by
-// row and thread i takes chunks i, i + 256, ...: consecutive threads copy
-// consecutive chunks of a row, so a warp's copies cover two rows' spans
-// contiguously.
-template <typename L>
-__device__ __forceinline__ void issue_row_copies(const uint8_t* table, uint32_t sbase, int stage, int tid,
-                                                 uint32_t full0) {
-    const uint32_t dst0 = sbase + L::x_off + stage * L::stage_bytes;
-    constexpr int kChunks = kRowSlot / 16;
-#pragma unroll 3
-    for (int item = tid; item < kTileRows * kChunks; item += kComputeThreads) {
-        const int row = item / kChunks;
-        const int chunk = item - row * kChunks;
-        const uint4 e = *reinterpret_cast<const uint4*>(table + row * 16);  // {src lo, src hi, bytes, -}
-        const uint64_t src = ((uint64_t)e.y << 32) | e.x;
-        const uint32_t bytes = e.z;
-        if ((uint32_t)chunk * 16u < bytes)
-            cp_async_16(dst0 + row * kRowSlot + chunk * 16, reinterpret_cast<const void*>(src + chunk * 16));
+// Issue the TMA loads of tile (rt, ct) into the stage at shared address dst.
+template <bool ROWS>
+__device__ __forceinline__ void load_tile(const XMaps<ROWS>& xm, const TmaParams& p, uint32_t dst, int rt, int ct,
+                                          uint32_t full) {
+    if constexpr (ROWS) {
+        mbar_arrive_expect_tx(full, (uint32_t)(p.n_phases * kPhaseBoxBytes));
+        for (int f = 0; f < p.n_phases; ++f)
+            tma_load_2d(dst + f * kPhaseBoxBytes, &xm.map[f], ct * kTileCols, rt * kPhaseRows, full);
+    } else {
+        mbar_arrive_expect_tx(full, kStageBytes);
+        tma_load_2d(dst, &xm.map[0], ct * kTileCols, rt * kTileRows, full);
+        tma_load_2d(dst + kBoxBytes, &xm.map[0], ct * kTileCols + kBoxCols, rt * kTileRows, full);
     }
-    cp_async_arrive(full0 + 8 * stage);
 }
 
-// Row path (ROWS = true): for X whose rows are not 16-byte aligned (odd K,
-// 2-byte aligned views), which no tensor map can describe.  The compute
-// threads copy, for the tile STAGES ahead, each row's 16-byte aligned span
-// around the tile's 128 columns with 16-byte cp.async copies (consecutive
-// threads on consecutive chunks of a row), and each arrives on that stage's
-// barrier when its copies land.  The compute threads then re-align their 64
-// elements in registers (read_row_words) and zero everything outside (m, k).
-// A span never leaves the 16-byte chunks that hold the row's own elements,
-// so no copy touches a page outside X.
-//
-// Measured on B200 at 8192 x 8191 bf16 (TB/s, one GPU call per line):
-//   plain-load kernel (quantize_generic.cu) 2.55; one producer warp issuing
-//   per-row bulk copies or cp.async copies 1.5 (too few in flight); each
-//   thread copying its own row 2.45; coalesced copies by all compute threads
-//   2.97, with the span table 3.06;
-//   + mask-free re-align when the 64 columns are inside K 3.33, + one 16-byte
-//   table read 3.41, + 2 CTAs/SM with 2 stages 4.27 (3.82 alone);
-//   + 16-byte shared loads instead of 4-byte ones (4-way bank conflicts) 4.80.
+template <bool ROWS>
+__device__ __forceinline__ void prefetch_tile(const XMaps<ROWS>& xm, const TmaParams& p, int rt, int ct) {
+    if constexpr (ROWS) {
+        for (int f = 0; f < p.n_phases; ++f) tma_prefetch_l2_2d(&xm.map[f], ct * kTileCols, rt * kPhaseRows);
+    } else {
+        tma_prefetch_l2_2d(&xm.map[0], ct * kTileCols, rt * kTileRows);
+        tma_prefetch_l2_2d(&xm.map[0], ct * kTileCols + kBoxCols, rt * kTileRows);
+    }
+}
+
 template <int DT, int STAGES, bool ROWS>
 __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
-    quantize_tma_kernel(const __grid_constant__ CUtensorMap xmap, const TmaParams p) {
+    quantize_tma_kernel(const __grid_constant__ XMaps<ROWS> xm, const TmaParams p) {
     using L = Layout<STAGES, ROWS>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // Pointer arithmetic on the __shared__ array (not integer casts) keeps the
@@ -259,22 +261,21 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
 
     if (tid == 0) {
         for (int i = 0; i < STAGES; ++i) {
-            mbar_init(full0 + 8 * i, ROWS ? kComputeThreads : 1);  // row path: one arrival per compute thread
+            mbar_init(full0 + 8 * i, 1);
             mbar_init(empty0 + 8 * i, kComputeWarps);
         }
         ctl[0] = 0;
         ctl[1] = 0;
         fence_mbar_init();
     }
-    if (!ROWS && tid == kComputeThreads) prefetch_tensormap(&xmap);
+    if (tid == kComputeThreads) {
+        for (int f = 0; f < (ROWS ? p.n_phases : 1); ++f) prefetch_tensormap(&xm.map[f]);
+    }
     __syncthreads();
-    if (!ROWS && tid == kComputeThreads) {
+    if (tid == kComputeThreads) {
         for (int i = 0, t = blockIdx.x; i < kPrefetchTiles && t < p.n_tiles; ++i, t += gridDim.x) {
             const int rt_local = t / p.n_col_tiles;
-            const int ct = t - rt_local * p.n_col_tiles;
-            const int rt = rt_local + p.rt_offset;
-            tma_prefetch_l2_2d(&xmap, ct * kTileCols, rt * kTileRows);
-            tma_prefetch_l2_2d(&xmap, ct * kTileCols + kBoxCols, rt * kTileRows);
+            prefetch_tile<ROWS>(xm, p, rt_local + p.rt_offset, t - rt_local * p.n_col_tiles);
         }
     }
     // Nothing above loaded or stored global data; everything below may read X
@@ -283,9 +284,7 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
     grid_wait_prerequisites();
 
     int issued = 0;
-    if (ROWS && warp == kComputeWarps) {
-        // row path: the compute threads issue their own copies (below)
-    } else if (warp == kComputeWarps) {
+    if (warp == kComputeWarps) {
         // ---------------- producer: one lane streams X tiles ----------------
         if (lane == 0) {
             int it = 0;
@@ -309,30 +308,16 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
                 }
                 const int rt_local = t / p.n_col_tiles;
                 const int ct = t - rt_local * p.n_col_tiles;
-                const int rt = rt_local + p.rt_offset;
-                const uint32_t full = full0 + 8 * stage;
-                const uint32_t dst = sbase + L::x_off + stage * L::stage_bytes;
-                mbar_arrive_expect_tx(full, kStageBytes);
-                tma_load_2d(dst, &xmap, ct * kTileCols, rt * kTileRows, full);
-                tma_load_2d(dst + kBoxBytes, &xmap, ct * kTileCols + kBoxCols, rt * kTileRows, full);
+                load_tile<ROWS>(xm, p, sbase + L::x_off + stage * L::stage_bytes, rt_local + p.rt_offset, ct,
+                                full0 + 8 * stage);
             }
             issued = it;
         }
     } else {
         // ---------------- compute warps ----------------
-        const int r = tid & (kTileRows - 1);  // row inside the tile
-        const int h = tid >> 7;               // which box / pair of scale blocks
-        const uint32_t swz = (uint32_t)(r & 7);
-        if constexpr (ROWS) {
-            // fill the ring: tiles 0 .. STAGES-1 of this CTA
-            uint8_t* table = smem + L::span_off;
-            for (int j = 0, t = blockIdx.x; j < STAGES && t < p.n_tiles; ++j, t += gridDim.x) {
-                write_row_span(p, table, t, tid);
-                named_bar_sync(kBarCompute, kComputeThreads);
-                issue_row_copies<L>(table, sbase, j, tid, full0);
-                named_bar_sync(kBarCompute, kComputeThreads);
-            }
-        }
+        const int r = tile_row<ROWS>(tid);   // row inside the tile
+        const int h = tid >> 7;              // which box / pair of scale blocks
+        const uint32_t swz = stage_key<ROWS>(r);
         int it = 0;
         for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++it) {
             const int stage = it % STAGES;
@@ -346,8 +331,9 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
             if (ok) {
                 uint32_t w0[16], w1[16];
                 if constexpr (ROWS) {
-                    read_row_words(p, smem + L::x_off + stage * L::stage_bytes + r * kRowSlot,
-                                   rt * kTileRows + r, ct * kTileCols, h, w0, w1);
+                    const uint8_t* slot = smem + L::x_off + stage * L::stage_bytes + (r & 7) * kPhaseBoxBytes +
+                                          (r >> 3) * kRowSlot;
+                    read_row_words(p, slot, rt * kTileRows + r, ct * kTileCols, h, w0, w1);
                 } else {
                     const uint8_t* xrow = smem + L::x_off + stage * kStageBytes + h * kBoxBytes + r * 128;
 #pragma unroll
@@ -359,10 +345,8 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
                     }
                 }
                 // X reads of this stage are done: release it to the producer.
-                if constexpr (!ROWS) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(empty0 + 8 * stage);
-                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty0 + 8 * stage);
 
                 uint32_t q0[8], q1[8];
                 uint32_t b0 = quantize_block<DT>(w0, q0);
@@ -383,12 +367,6 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
                 *reinterpret_cast<uint16_t*>(smem + L::s_off + qb * kSChunkBytes + (r & 31) * 16 + (r >> 5) * 4 +
                                              2 * h) = static_cast<uint16_t>(b0 | (b1 << 8));
             }
-            if constexpr (ROWS) {
-                // spans of the tile STAGES ahead, for the copies after the barrier
-                // (two tables: a slow thread may still read the other one)
-                const int tn = t + STAGES * gridDim.x;
-                if (tn < p.n_tiles) write_row_span(p, smem + L::span_off + (it & 1) * kTileRows * 16, tn, tid);
-            }
             // Publishes staging buffer qb.  Buffer qb is written again two
             // tiles later, after the next barrier, which every thread reaches
             // only once its stores below have read the buffer.
@@ -399,18 +377,12 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
                 }
                 break;
             }
-            if constexpr (ROWS) {
-                // every thread has read this stage: refill it with the tile STAGES ahead
-                const int tn = t + STAGES * gridDim.x;
-                if (tn < p.n_tiles)
-                    issue_row_copies<L>(smem + L::span_off + (it & 1) * kTileRows * 16, sbase, stage, tid, full0);
-            }
             const uint8_t* qbuf = smem + L::q_off + qb * kQTileBytes;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int row = warp * 16 + i * 4 + (lane >> 3);
                 const int chunk = lane & 7;
-                const uint4 v = *reinterpret_cast<const uint4*>(qbuf + row * 128 + ((chunk ^ (row & 7)) << 4));
+                const uint4 v = *reinterpret_cast<const uint4*>(qbuf + row * 128 + ((chunk ^ stage_key<ROWS>(row)) << 4));
                 const int grow = rt * kTileRows + row;
                 const int col = ct * kTileCols + chunk * 16;  // q_cols % 32 == 0: a chunk is all in or all out
                 if (grow < p.q_rows && col < p.q_cols)
@@ -422,8 +394,6 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
             }
         }
         if (tid == 0) ctl[1] = it;
-        // row path: this thread's copies still in flight (only after an abort) land before exit
-        if constexpr (ROWS) asm volatile("cp.async.wait_all;" ::: "memory");
     }
     __syncthreads();
     if (warp == kComputeWarps && lane == 0) {
@@ -459,8 +429,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     return fn;
 }
 
-static int encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t cols, uint64_t rows,
-                     uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows) {
+static int encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride_bytes,
+                     uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
     auto encode = get_encode_fn();
     if (!encode) {
         set_last_error("cuTensorMapEncodeTiled entry point unavailable", 0);
@@ -470,14 +440,37 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* bas
     cuuint64_t strides[1] = {row_stride_bytes};
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_last_error("cuTensorMapEncodeTiled failed", (int)r);
         return MXFP8_ERR_TENSOR_MAP;
     }
     return MXFP8_OK;
+}
+
+// Tensor maps of X.  Tensor path: one map, 64 x 128 boxes, 128-byte swizzle.
+// Row path: one map per phase f < min(m, 8) (see the file comment).
+template <bool ROWS>
+static int encode_x_maps(const QuantizeArgs& a, XMaps<ROWS>& xm) {
+    memset(&xm, 0, sizeof(xm));
+    if constexpr (!ROWS) {
+        return encode_2d(&xm.map[0], a.x, (uint64_t)a.k, (uint64_t)a.m, (uint64_t)a.ld_x * 2, kBoxCols, kTileRows,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+        const int64_t phases = a.m < kPhases ? a.m : kPhases;
+        for (int64_t f = 0; f < phases; ++f) {
+            const uintptr_t row0 = reinterpret_cast<uintptr_t>(a.x) + (uintptr_t)(2 * f * a.ld_x);
+            const uintptr_t base = row0 & ~(uintptr_t)15;
+            const uint64_t d = (row0 - base) / 2;  // elements of misalignment, < 8
+            const uint64_t rows = (uint64_t)((a.m - f + kPhases - 1) / kPhases);
+            int rc = encode_2d(&xm.map[f], reinterpret_cast<const void*>(base), (uint64_t)a.k + d, rows,
+                               (uint64_t)a.ld_x * 2 * kPhases, kRowBoxCols, kPhaseRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (rc) return rc;
+        }
+        return MXFP8_OK;
+    }
 }
 
 template <int DT, bool ROWS>
@@ -502,18 +495,15 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
         set_last_error("cudaFuncSetAttribute", (int)e);
         return MXFP8_ERR_CUDA;
     }
-    CUtensorMap xmap;
-    memset(&xmap, 0, sizeof(xmap));  // the row path uses no tensor map
-    if (!ROWS) {
-        int rc = encode_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.x, (uint64_t)a.k, (uint64_t)a.m,
-                           (uint64_t)a.ld_x * 2, kBoxCols, kTileRows);
-        if (rc) return rc;
-    }
+    XMaps<ROWS> xm;
+    int rc = encode_x_maps<ROWS>(a, xm);
+    if (rc) return rc;
     TmaParams p;
     p.x = static_cast<const uint8_t*>(a.x);
     p.ld_x = a.ld_x;
     p.m = (int)a.m;
     p.k = (int)a.k;
+    p.n_phases = (int)(a.m < kPhases ? a.m : kPhases);
     const int64_t n_row_tiles = a.scale_rows / kTileRows;
     p.n_col_tiles = (int)a.col_chunks;
     p.q = a.q;
@@ -551,7 +541,7 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kernel, xmap, p);
+        e = cudaLaunchKernelEx(&cfg, kernel, xm, p);
         if (e == cudaSuccess) e = cudaGetLastError();
     }
     if (e != cudaSuccess) {
@@ -562,7 +552,7 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
 }
 
 int launch_quantize_tma(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
-    // rows a tensor map can describe: 16-byte aligned base and row stride
+    // rows a single tensor map can describe: 16-byte aligned base and row stride
     const bool tensor = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.ld_x % 8 == 0;
     if (a.dtype == kBF16)
         return tensor ? launch_tma_typed<kBF16, false>(a, sm_count, stream)

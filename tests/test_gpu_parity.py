@@ -396,6 +396,17 @@ def test_odd_layouts_special_values(m, k, x_offset, dtype, q_offset, capi, oracl
     check_against_oracle(capi, oracle_mod, bits, dtype, m, kk, x_offset=x_offset, q_offset=q_offset)
 
 
+@pytest.mark.parametrize("m", [1, 2, 3, 7, 8, 9, 15, 17, 130])
+def test_row_path_few_rows_every_offset(m, capi, oracle_mod):
+    """Row path with fewer than 8 rows (fewer tensor-map phases than 8) and
+    around multiples of 8, at every 2-byte offset of X and odd / even-not-8
+    row strides."""
+    for k, ld in ((33, 35), (300, 301), (130, 134)):
+        bits = inputs.normal(m, k, m * 1000 + k, "bf16", sigma=3.0)
+        for x_offset in range(8):
+            check_against_oracle(capi, oracle_mod, bits, "bf16", ld_x=ld, x_offset=x_offset)
+
+
 def test_three_kernels_agree_across_launch_split(capi):
     """38000 x 8191 bf16 (622 MB): the same X through the row path (row
     stride 8191, two launches: 296 row tiles + 1), the tensor path (row
