@@ -118,7 +118,7 @@ def cpu_oracle_time(x_bits, m_rows: int, k: int, reps: int, threads: int) -> flo
     best = float("inf")
     for _ in range(reps):
         t0 = time.perf_counter()
-        oracle.quantize(x_bits[:m_rows], "bf16", m_rows, k, nthreads=threads)
+        oracle.quantize(x_bits[:m_rows], "bf16", m_rows, -(-k // SCALE_VEC) * SCALE_VEC, nthreads=threads)
         best = min(best, time.perf_counter() - t0)
     return best
 
@@ -432,19 +432,24 @@ def main() -> None:
     # this rank's rows of the global (m * world) x k matrix: whole 128-row chunks
     r0, r1 = pkg.shard.row_shard(args.m * world, world, rank)
     m, k = r1 - r0, args.k
+    # Q geometry: K rounded up to whole scale blocks (K itself on the driver's
+    # line; an odd --k runs X through the kernel's unaligned-row path)
+    q_cols = -(-k // SCALE_VEC) * SCALE_VEC
+    if args.op == "dequantize" and q_cols != k:
+        raise SystemExit("--op dequantize needs --k a multiple of 32")
     nbytes = algo_bytes(m, k)
-    s_bytes = capi.scale_storage_bytes(m, k)
-    ws_bytes = 2 * m * k + m * k + s_bytes
+    s_bytes = capi.scale_storage_bytes(m, q_cols)
+    ws_bytes = 2 * m * k + m * q_cols + s_bytes
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     n_ws = max(2, math.ceil(3 * l2 / ws_bytes))
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     xs = [torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16) for _ in range(n_ws)]
-    qs = [torch.empty((m, k), dtype=torch.uint8, device=dev) for _ in range(n_ws)]
+    qs = [torch.empty((m, q_cols), dtype=torch.uint8, device=dev) for _ in range(n_ws)]
     ss = [torch.empty((s_bytes,), dtype=torch.uint8, device=dev) for _ in range(n_ws)]
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     lib = capi.lib()
-    launch_args = [(xs[i].data_ptr(), 0, m, k, k, qs[i].data_ptr(), m, k, k, ss[i].data_ptr(), s_bytes, sh)
+    launch_args = [(xs[i].data_ptr(), 0, m, k, k, qs[i].data_ptr(), m, q_cols, q_cols, ss[i].data_ptr(), s_bytes, sh)
                    for i in range(n_ws)]
 
     def launch(i):
@@ -463,7 +468,7 @@ def main() -> None:
     launch(0)
     torch.cuda.synchronize()
     buffers = {"x": xs[0], "q_fp8": qs[0].view(torch.float8_e4m3fn), "s_storage_bytes": ss[0]}
-    ver = pkg.verify_quantizer_outputs(buffers, m, k, m, k)
+    ver = pkg.verify_quantizer_outputs(buffers, m, q_cols, m, k)
     if not ver["verification_passed"] or ver["q_max_byte_diff"] != 0:
         raise SystemExit(f"verification failed on rank {rank}: {ver}")
 
@@ -511,7 +516,7 @@ def main() -> None:
     # end to end through the public API with host buffers: pinned X in, Q and S out
     x_host = torch.empty((m, k), dtype=torch.bfloat16, pin_memory=True)
     x_host.copy_(xs[0].cpu())
-    q_host = torch.empty((m, k), dtype=torch.uint8, pin_memory=True)
+    q_host = torch.empty((m, q_cols), dtype=torch.uint8, pin_memory=True)
     s_host = torch.empty((s_bytes,), dtype=torch.uint8, pin_memory=True)
     hq = pkg.HostQuantizer(m, k, torch.bfloat16, device=dev)
     for _ in range(2):
@@ -555,7 +560,7 @@ def main() -> None:
                      "peak_kind": peak_kind, "traffic": traffic,
                      "algorithmic_bytes_per_launch": nbytes},
         "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": 2 * m * k,
-                "d2h_bytes_per_step": m * k + s_bytes, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": m * q_cols + s_bytes, "ms_per_step": e2e_ms},
         "gpu_launches": args.steps,
         "verification": ver,
     })
