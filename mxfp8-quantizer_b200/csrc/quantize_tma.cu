@@ -89,8 +89,8 @@ constexpr int kPhaseBoxBytes = kPhaseRows * kRowSlot;     // 4352 (a multiple of
 constexpr int kRowStageBytes = kPhases * kPhaseBoxBytes;  // 34 KiB of X per tile
 // The row path's compute warps do more work per tile (the register shift), so
 // it runs 2 CTAs per SM with 2 stages each (~105 KiB of shared memory apiece)
-// for twice the warps: 8192 x 8191 bf16 5.92 vs 5.61 TB/s with 1 CTA x 3
-// stages (1 CTA x 4 stages 5.53, x 2 stages 4.92).
+// for twice the warps: 8192 x 8191 bf16 6.25 vs 5.99 TB/s with 1 CTA x 3
+// stages (1 CTA x 4 or x 2 stages: slower still).
 constexpr int kRowStages = 2;
 constexpr int kRowCtasPerSm = 2;
 
@@ -147,17 +147,19 @@ __device__ __forceinline__ void report(unsigned int* status, unsigned code) {
     if (status) atomicOr(status, code);
 }
 
-// Row of the tile that compute thread `tid` handles.  Tensor path: tid % 128.
-// Row path: the 8 lanes of a shared-memory phase take 8 rows of one tensor-map
-// phase (rows 8j + f, consecutive j), whose 272-byte box rows start in 8
-// different 16-byte bank groups, so the X reads stay conflict-free.
+// Row of the tile that compute thread `tid` handles, and which 64 of its 128
+// columns (h).  Tensor path: row tid % 128, h = tid / 128.  Row path: warp w
+// takes the 16 rows 8j + w of tensor-map phase w, lane l row j = l % 16 and
+// h = l / 16, so a warp shares one misalignment (warp-uniform re-align code)
+// and the 8 lanes of a shared-memory phase read 8 consecutive box rows of
+// 272 bytes, which start in 8 different 16-byte bank groups: conflict-free.
 template <bool ROWS>
 __device__ __forceinline__ int tile_row(int tid) {
-    const int t = tid & (kTileRows - 1);
-    if (!ROWS) return t;
-    const int j = (t & 7) | ((t >> 6) << 3);
-    const int f = (t >> 3) & 7;
-    return j * kPhases + f;
+    return ROWS ? (tid & 15) * kPhases + (tid >> 5) : (tid & (kTileRows - 1));
+}
+template <bool ROWS>
+__device__ __forceinline__ int tile_half(int tid) {
+    return ROWS ? (tid >> 4) & 1 : tid >> 7;
 }
 
 // XOR key of the payload staging buffer's 128-byte swizzle for tile row r:
@@ -167,14 +169,24 @@ __device__ __forceinline__ uint32_t stage_key(int r) {
     return ROWS ? (uint32_t)((r >> 3) & 7) : (uint32_t)(r & 7);
 }
 
+// Words W .. W+32 of v, shifted down by a further 2 bytes when sel says so.
+template <int W>
+__device__ __forceinline__ void shift_words(const uint32_t (&v)[36], uint32_t sel, uint32_t (&w0)[16],
+                                            uint32_t (&w1)[16]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const uint32_t x = __byte_perm(v[W + i], v[W + i + 1], sel);
+        if (i < 16) w0[i] = x; else w1[i - 16] = x;
+    }
+}
+
 // Row path: this thread's 64 elements (columns c0 + 64h ..) of row `row` from
 // its 272-byte box row, re-aligned to 16-bit lanes and zeroed outside (m, k).
-// Column c0 sits `off` bytes into the box row (off < 16, even).  The thread
-// loads the 9 aligned 16-byte words from byte 128h on (conflict-free, see
-// tile_row), then shifts them down by off bytes in registers: by 8 bytes, by
-// 4 bytes, then a byte permute.  4-byte loads from byte off & ~3 instead save
-// the selects but conflict whenever the rows of a warp share their word
-// offset (2-byte aligned views with ld_x % 8 == 0: 5.46 vs 6.02 TB/s).
+// Column c0 sits `off` bytes into the box row (off < 16, even, the same for
+// the whole warp).  The thread loads the 9 aligned 16-byte words from byte
+// 128h on, then takes 32 words from word off / 4 on, each a byte permute of
+// two neighbours (a 2-byte shift when off % 4 == 2).  Warp-uniform branches
+// pick the word offset, so no per-word selects are needed.
 __device__ __forceinline__ void read_row_words(const TmaParams& p, const uint8_t* slot, int row, int c0, int h,
                                                uint32_t (&w0)[16], uint32_t (&w1)[16]) {
     const int cf = c0 + 64 * h;
@@ -192,28 +204,21 @@ __device__ __forceinline__ void read_row_words(const TmaParams& p, const uint8_t
         const uint4 t = *reinterpret_cast<const uint4*>(slot + 128 * h + 16 * i);
         v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
     }
-    uint32_t u[34], raw[33];
-#pragma unroll
-    for (int i = 0; i < 34; ++i) u[i] = (off & 8u) ? v[i + 2] : v[i];
-#pragma unroll
-    for (int i = 0; i < 33; ++i) raw[i] = (off & 4u) ? u[i + 1] : u[i];
     const uint32_t sel = (off & 2u) ? 0x5432u : 0x3210u;
-    // Two loops, not one with a per-word test: 4.78 vs 4.16 TB/s at 8192 x 8191.
-    if (cf + 64 <= p.k) {  // all 64 columns inside K (the same for the whole warp)
+    switch (off >> 2) {
+        case 0: shift_words<0>(v, sel, w0, w1); break;
+        case 1: shift_words<1>(v, sel, w0, w1); break;
+        case 2: shift_words<2>(v, sel, w0, w1); break;
+        default: shift_words<3>(v, sel, w0, w1); break;
+    }
+    if (cf + 64 > p.k) {  // the columns cross K (the same for the whole warp)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-            const uint32_t x = __byte_perm(raw[i], raw[i + 1], sel);
-            if (i < 16) w0[i] = x; else w1[i - 16] = x;
+            const int c = cf + 2 * i;
+            uint32_t& x = i < 16 ? w0[i] : w1[i - 16];
+            if (c >= p.k) x = 0u;
+            else if (c + 1 >= p.k) x &= 0xFFFFu;
         }
-        return;
-    }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        uint32_t x = __byte_perm(raw[i], raw[i + 1], sel);
-        const int c = cf + 2 * i;
-        if (c >= p.k) x = 0u;
-        else if (c + 1 >= p.k) x &= 0xFFFFu;
-        if (i < 16) w0[i] = x; else w1[i - 16] = x;
     }
 }
 
@@ -316,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
     } else {
         // ---------------- compute warps ----------------
         const int r = tile_row<ROWS>(tid);   // row inside the tile
-        const int h = tid >> 7;              // which box / pair of scale blocks
+        const int h = tile_half<ROWS>(tid);  // which 64 columns / pair of scale blocks
         const uint32_t swz = stage_key<ROWS>(r);
         int it = 0;
         for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++it) {
@@ -414,6 +419,10 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
 
 constexpr int kStages = 3;
 constexpr int64_t kMaxTilesPerLaunch = 148 * 128;  // ~0.94 GB of traffic per launch
+// The row path's two CTAs per SM drift apart sooner: above ~8k tiles its
+// launch times turned bimodal (16384 x 16383: min 6.43, median 5.68 TB/s);
+// split at 148 x 64 tiles, median 6.40, no change at 8192 tiles or below.
+constexpr int64_t kMaxTilesPerLaunchRows = 148 * 64;
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -521,8 +530,9 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
     // in step every ~0.9 GB measured 6.77 vs 6.35 TB/s at 131072x16384 and
     // changed nothing at 16384^2 or below.
     int64_t rows_per_launch = n_row_tiles;
-    if (n_row_tiles * a.col_chunks > kMaxTilesPerLaunch) {
-        rows_per_launch = kMaxTilesPerLaunch / a.col_chunks;
+    const int64_t max_tiles = ROWS ? kMaxTilesPerLaunchRows : kMaxTilesPerLaunch;
+    if (n_row_tiles * a.col_chunks > max_tiles) {
+        rows_per_launch = max_tiles / a.col_chunks;
         if (rows_per_launch < 1) rows_per_launch = 1;
     }
     for (int64_t r0 = 0; r0 < n_row_tiles && e == cudaSuccess; r0 += rows_per_launch) {

@@ -409,9 +409,10 @@ def test_row_path_few_rows_every_offset(m, capi, oracle_mod):
 
 def test_three_kernels_agree_across_launch_split(capi):
     """38000 x 8191 bf16 (622 MB): the same X through the row path (row
-    stride 8191, two launches: 296 row tiles + 1), the tensor path (row
-    stride 8192) and the plain-load kernel (Q 8 bytes off 16-byte alignment)
-    gives identical Q and S bytes, in the reference geometry."""
+    stride 8191, three launches of 148 + 148 + 1 row tiles), the tensor path
+    (row stride 8192, two launches of 296 + 1 row tiles) and the plain-load
+    kernel (Q 8 bytes off 16-byte alignment) gives identical Q and S bytes,
+    in the reference geometry."""
     m, k = 38000, 8191
     q_rows, q_cols = (m + 7) // 8 * 8, (k + 255) // 256 * 256
     s_bytes = capi.scale_storage_bytes(q_rows, q_cols)
