@@ -191,10 +191,9 @@ extern "C" MXFP8_API int mxfp8_quantize_noalloc(const void* x, int dtype, int64_
         return MXFP8_ERR_DEVICE;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const bool tma_ok = has_x && aligned(x, 16) && ld_x % 8 == 0 && aligned(q, 16) && ld_q % 16 == 0 &&
-                        aligned(s, 16);
-    // The plain-load kernel uses no scratch, so it runs unchanged.
-    return tma_ok ? launch_quantize_tma_noalloc(a, dev, sms, st) : launch_quantize_generic(a, sms, st);
+    // Same dispatch as mxfp8_quantize; the plain-load kernel uses no scratch.
+    const bool out_ok = has_x && aligned(q, 16) && ld_q % 16 == 0 && aligned(s, 16);
+    return out_ok ? launch_quantize_tma_noalloc(a, dev, sms, st) : launch_quantize_generic(a, sms, st);
 }
 
 extern "C" MXFP8_API int mxfp8_quantize_padded(const void* x, void* q_dwords, void* s_words, int64_t m, int64_t k,

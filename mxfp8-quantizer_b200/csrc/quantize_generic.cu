@@ -1,7 +1,6 @@
 // quantize_generic.cu -- MXFP8 quantizer for layouts the pipelined kernel
 // (quantize_tma.cu) does not take: Q rows or S that are not 16-byte aligned,
-// empty X, and, for the allocation-free entry point, X rows that are not
-// 16-byte aligned.  Same recipe (recipe.cuh) and output contract.
+// and empty X.  Same recipe (recipe.cuh) and output contract.
 //
 // Work item: 4 rows x one 256-column segment (8 scale blocks), one warp.
 // Lane l owns columns [8l, 8l + 8) of the segment, so a quad of lanes holds

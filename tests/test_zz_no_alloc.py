@@ -45,6 +45,8 @@ CASES = [
     # reference's padded geometry, then a different shape and dtype
     (lambda: inputs.special_values_bf16(), "bf16", 1000, 4096),
     (lambda: inputs.normal(2051, 2080, 14, "fp16"), "fp16", 2056, 2304),
+    # odd K: X rows are not 16-byte aligned (the per-phase tensor-map path)
+    (lambda: inputs.normal(1001, 4095, 15, "bf16"), "bf16", 1001, 4096),
 ]
 
 
