@@ -68,6 +68,17 @@ int current_device(DeviceState** out) {
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+// Kernel choice, shared by both quantize entries.  The pipelined kernel needs
+// 16-byte aligned Q rows and S; it reads X through one tensor map when X's
+// rows are 16-byte aligned and through one tensor map per row phase
+// (row % 8) otherwise.  Row phases are 16 * ld_x bytes apart and a tensor-map
+// stride must stay below 2^40 bytes, so larger strides of unaligned rows (only
+// reachable with sparse address reservations) take the plain-load kernel.
+bool use_pipelined(const void* x, int64_t ld_x, bool has_x, const void* q, int64_t ld_q, const void* s) {
+    const bool x_ok = (aligned(x, 16) && ld_x % 8 == 0) || ld_x < (int64_t(1) << 36);
+    return has_x && x_ok && aligned(q, 16) && ld_q % 16 == 0 && aligned(s, 16);
+}
+
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace
@@ -136,11 +147,8 @@ extern "C" MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int
     if (rc) return rc;
     a.status = dev->status;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // The pipelined kernel needs 16-byte aligned Q rows and S; it reads X
-    // through one tensor map when X's rows are 16-byte aligned and through
-    // one tensor map per row phase (row % 8) otherwise.
-    const bool out_ok = has_x && aligned(q, 16) && ld_q % 16 == 0 && aligned(s, 16);
-    return out_ok ? launch_quantize_tma(a, dev->sm_count, st) : launch_quantize_generic(a, dev->sm_count, st);
+    return use_pipelined(x, ld_x, has_x, q, ld_q, s) ? launch_quantize_tma(a, dev->sm_count, st)
+                                                     : launch_quantize_generic(a, dev->sm_count, st);
 }
 
 // Allocation-free entry: the same argument checks and kernels as
@@ -192,8 +200,8 @@ extern "C" MXFP8_API int mxfp8_quantize_noalloc(const void* x, int dtype, int64_
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // Same dispatch as mxfp8_quantize; the plain-load kernel uses no scratch.
-    const bool out_ok = has_x && aligned(q, 16) && ld_q % 16 == 0 && aligned(s, 16);
-    return out_ok ? launch_quantize_tma_noalloc(a, dev, sms, st) : launch_quantize_generic(a, sms, st);
+    return use_pipelined(x, ld_x, has_x, q, ld_q, s) ? launch_quantize_tma_noalloc(a, dev, sms, st)
+                                                     : launch_quantize_generic(a, sms, st);
 }
 
 extern "C" MXFP8_API int mxfp8_quantize_padded(const void* x, void* q_dwords, void* s_words, int64_t m, int64_t k,
