@@ -407,6 +407,21 @@ def test_row_path_few_rows_every_offset(m, capi, oracle_mod):
             check_against_oracle(capi, oracle_mod, bits, "bf16", ld_x=ld, x_offset=x_offset)
 
 
+@pytest.mark.parametrize("m,k,dtype,geometry", [
+    (1, 65535 * 256, "bf16", "reference"),      # the reference's widest launch (65535 K-tiles), tensor path
+    (3, 65535 * 256 - 1, "fp16", "tight"),      # as wide, odd K: per-phase tensor maps, 3 phases
+    (1 << 20, 32, "fp16", "reference"),        # one scale block per row, 8192 row tiles
+    (100003, 33, "bf16", "tight"),             # tall with odd K: row path, ragged last row tile
+])
+def test_extreme_aspect_ratios(m, k, dtype, geometry, capi, oracle_mod):
+    """Very wide and very tall X against the oracle, byte for byte."""
+    bits = inputs.normal(m, k, m + k, dtype, sigma=5.0)
+    if geometry == "reference":
+        check_against_oracle(capi, oracle_mod, bits, dtype)
+    else:
+        check_against_oracle(capi, oracle_mod, bits, dtype, m, (k + 31) // 32 * 32)
+
+
 def test_three_kernels_agree_across_launch_split(capi):
     """38000 x 8191 bf16 (622 MB): the same X through the row path (row
     stride 8191, three launches of 148 + 148 + 1 row tiles), the tensor path
