@@ -41,6 +41,19 @@ def algo_bytes(m: int, k: int) -> int:
     return 2 * m * k + m * k + m * (k // SCALE_VEC)
 
 
+def launches_per_call(m: int, k: int, ld_x: int) -> int:
+    """Kernel launches one mxfp8_quantize call makes: the pipelined kernel
+    splits problems of more than 148*128 tiles (148*64 on its unaligned-row
+    path) into launches of whole 128-row tiles, mirroring kMaxTilesPerLaunch
+    and kMaxTilesPerLaunchRows in csrc/quantize_tma.cu.  X is assumed
+    16-byte aligned (torch allocations are)."""
+    col_tiles = -(-(-(-k // SCALE_VEC)) // 4)
+    row_tiles = -(-m // 128)
+    max_tiles = 148 * 128 if ld_x % 8 == 0 else 148 * 64
+    rows_per_launch = max(1, max_tiles // col_tiles) if row_tiles * col_tiles > max_tiles else row_tiles
+    return -(-row_tiles // rows_per_launch)
+
+
 def measured_hbm_peak() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -371,6 +384,7 @@ def c5_arm(args, rank: int, world: int, local: int) -> None:
             "warmup": args.warmup, "ms_per_step": slowest, "fastest_rank_ms": fastest,
             "per_gpu_tb_s": algo_bytes(m, k) / (slowest * 1e-3) / 1e12, "higher_is_better": True,
             "scaling": "strong", "dtype": "f32", "data": "synthetic: N(0,2) bf16 from per-1024-row-block seeds",
+            "gpu_launches": steps * launches_per_call(m, k, k),
             "config": {"workload": f"131072x16384 bf16, rows [{r0}, {r1}) on rank 0 of {world}",
                        "parallelism": f"row shards of 128-row chunks x{world}, no collective"}}), flush=True)
 
@@ -561,7 +575,7 @@ def main() -> None:
                      "algorithmic_bytes_per_launch": nbytes},
         "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": 2 * m * k,
                 "d2h_bytes_per_step": m * q_cols + s_bytes, "ms_per_step": e2e_ms},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * launches_per_call(m, k, k),
         "verification": ver,
     })
     if cpu is not None:

@@ -38,3 +38,19 @@ def test_reference_arm_is_silent_on_nonzero_ranks():
     lines = run_bench("--impl", "reference", "--m", "256", "--k", "256", "--steps", "1", "--warmup", "3",
                       env_extra={"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert lines == []
+
+
+def test_launches_per_call_follows_the_split_rule():
+    """bench.py's gpu_launches count: one launch up to 148*128 tiles (148*64
+    for X rows that are not 16-byte aligned), then whole 128-row tiles per
+    launch.  The GPU suite checks the same numbers against profiler counts."""
+    import bench
+
+    assert bench.launches_per_call(8192, 8192, 8192) == 1
+    assert bench.launches_per_call(8192, 8191, 8191) == 1
+    assert bench.launches_per_call(32768, 16384, 16384) == 2
+    assert bench.launches_per_call(131072, 16384, 16384) == 7
+    assert bench.launches_per_call(16384, 16383, 16383) == 2
+    assert bench.launches_per_call(38000, 8192, 8192) == 2
+    assert bench.launches_per_call(38000, 8191, 8191) == 3
+    assert bench.launches_per_call(1, 65535 * 256, 65535 * 256) == 1

@@ -309,22 +309,23 @@ def test_bounded_wait_times_out_and_reports(capi, golden):
     assert sha(q) == golden["cases"]["c1"]["q_sha256"] and sha(s) == golden["cases"]["c1"]["s_sha256"]
 
 
-def test_host_quantizer_matches_device_path(capi, oracle_mod):
+@pytest.mark.parametrize("m,k,dtype", [(2500, 1000, "fp16"), (1300, 777, "bf16")])
+def test_host_quantizer_matches_device_path(m, k, dtype, capi, oracle_mod):
     """HostQuantizer (pinned host X in, host Q/S out, row chunks over three
-    streams) gives the bytes of the device path, for a ragged row count."""
+    streams) gives the bytes of the device path, for a ragged row count; odd
+    K takes the device's per-phase tensor-map path."""
     import MXFP8_quantizer
 
     pkg = MXFP8_quantizer.load_package()
-    m, k = 2500, 1000
-    bits = inputs.normal(m, k, 55, "fp16", sigma=4.0)
-    x_host = inputs.bits_to_torch(bits, "fp16").pin_memory()
-    hq = pkg.HostQuantizer(m, k, torch.float16, chunk_rows=512)
+    bits = inputs.normal(m, k, 55, dtype, sigma=4.0)
+    x_host = inputs.bits_to_torch(bits, dtype).pin_memory()
+    hq = pkg.HostQuantizer(m, k, torch.float16 if dtype == "fp16" else torch.bfloat16, chunk_rows=512)
     q_host = torch.empty((m, hq.q_cols), dtype=torch.uint8).pin_memory()
     s_host = torch.empty((hq.s_bytes,), dtype=torch.uint8).pin_memory()
     for _ in range(2):
         hq(x_host, q_host, s_host)
     torch.cuda.synchronize()
-    q_ref, s_ref = oracle_mod.quantize(bits, "fp16", m, hq.q_cols)
+    q_ref, s_ref = oracle_mod.quantize(bits, dtype, m, hq.q_cols)
     assert np.array_equal(q_host.numpy(), q_ref)
     assert np.array_equal(s_host.numpy(), s_ref)
 
@@ -420,6 +421,29 @@ def test_extreme_aspect_ratios(m, k, dtype, geometry, capi, oracle_mod):
         check_against_oracle(capi, oracle_mod, bits, dtype)
     else:
         check_against_oracle(capi, oracle_mod, bits, dtype, m, (k + 31) // 32 * 32)
+
+
+@pytest.mark.parametrize("m,k", [(8192, 8192), (38000, 8192), (38000, 8191), (16384, 16383)])
+def test_launch_count_matches_bench_accounting(m, k, capi):
+    """The kernel launches one call makes, counted by the CUDA profiler,
+    equal bench.py's gpu_launches rule (the launch split by tile count)."""
+    import bench
+    from torch.profiler import ProfilerActivity, profile
+
+    q_cols = (k + 31) // 32 * 32
+    s_bytes = capi.scale_storage_bytes(m, q_cols)
+    x = torch.zeros((m, k), dtype=torch.bfloat16, device="cuda")
+    q = torch.empty((m, q_cols), dtype=torch.uint8, device="cuda")
+    s = torch.empty((s_bytes,), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    args = (x.data_ptr(), 0, m, k, k, q.data_ptr(), m, q_cols, q_cols, s.data_ptr(), s_bytes, stream)
+    capi.quantize(*args)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
+        capi.quantize(*args)
+        torch.cuda.synchronize()
+    launches = sum(1 for e in prof.events() if "quantize_tma_kernel" in e.name)
+    assert launches == bench.launches_per_call(m, k, k)
 
 
 def test_three_kernels_agree_across_launch_split(capi):
