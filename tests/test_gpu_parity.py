@@ -118,9 +118,13 @@ def test_special_values_c4(geometry, capi, oracle_mod):
         check_against_oracle(capi, oracle_mod, bits, "bf16", 1000, 4064)
 
 
+@pytest.mark.parametrize("layout", ["aligned", "unaligned_rows"])
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
-def test_special_values_every_nonfinite_pattern(dtype, capi, oracle_mod):
-    check_against_oracle(capi, oracle_mod, inputs.nonfinite_patterns(dtype), dtype)
+def test_special_values_every_nonfinite_pattern(dtype, layout, capi, oracle_mod):
+    """Every inf/NaN pattern, through one tensor map (aligned X) and through
+    the per-row-phase maps (row stride 37, X 6 bytes past a 16-byte boundary)."""
+    kw = {} if layout == "aligned" else dict(ld_x=37, x_offset=3)
+    check_against_oracle(capi, oracle_mod, inputs.nonfinite_patterns(dtype), dtype, **kw)
 
 
 SHAPES = [(1, 1), (1, 32), (2, 64), (7, 33), (8, 256), (9, 255), (127, 129), (128, 128), (129, 4064),
@@ -472,6 +476,30 @@ def test_three_kernels_agree_across_launch_split(capi):
     for q, s in outs[1:]:
         assert torch.equal(q, outs[0][0]) and torch.equal(s, outs[0][1])
     assert capi.device_status(clear=True) == 0
+
+
+def test_randomized_unaligned_x(capi, oracle_mod):
+    """150 seeded random cases whose X rows are not 16-byte aligned (the
+    per-row-phase tensor maps): shape, dtype, row stride, 2-byte offset,
+    geometry and value distribution."""
+    rng = np.random.default_rng(77)
+    for case in range(150):
+        m = int(rng.integers(1, 600))
+        k = int(rng.integers(1, 2000))
+        dtype = "bf16" if rng.random() < 0.5 else "fp16"
+        ld = k + int(rng.integers(0, 10))
+        x_offset = int(rng.integers(0, 8))
+        if ld % 8 == 0 and x_offset == 0:
+            ld += 1
+        if rng.random() < 0.3 and dtype == "bf16":
+            kk = (k + 31) // 32 * 32
+            bits = inputs.special_values_bf16(m, kk, seed=case)[:, :k].copy()
+        else:
+            bits = inputs.normal(m, k, 1000 + case, dtype, sigma=float(10 ** rng.uniform(-2, 2)))
+        if rng.random() < 0.5:
+            check_against_oracle(capi, oracle_mod, bits, dtype, ld_x=ld, x_offset=x_offset)
+        else:
+            check_against_oracle(capi, oracle_mod, bits, dtype, m, (k + 31) // 32 * 32, ld_x=ld, x_offset=x_offset)
 
 
 def test_randomized_shapes_layouts_and_values(capi, oracle_mod):
