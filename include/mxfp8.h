@@ -69,10 +69,12 @@ MXFP8_API int mxfp8_launch_shape(int64_t m, int64_t k, int64_t* kernel_m, int64_
  * the next multiple of 4) are written as 0.  Every byte of
  * Q[0:q_rows, 0:q_cols] and of the first mxfp8_scale_storage_bytes(q_rows,
  * q_cols) bytes of S is written; nothing needs zeroing beforehand.
- * Fast path (TMA, persistent): q and s 16-byte aligned, ld_q % 16 == 0.  It
+ * Every non-empty x runs through one persistent TMA-pipelined kernel: it
  * reads x through one tensor map when x is 16-byte aligned and ld_x % 8 ==
- * 0, else through one tensor map per row phase (row % 8).  Otherwise a
- * plain-load kernel runs.
+ * 0, else through one tensor map per row phase (row % 8), and writes q and s
+ * at any offset (16-byte stores when q, ld_q and s allow them, narrower or
+ * realigned stores otherwise).  Empty x (m or k == 0) takes a plain-load
+ * kernel that writes the padding.
  * The first call on a device allocates that device's 256-byte status word
  * (see mxfp8_device_status), so make it before any stream capture; later
  * calls allocate nothing.

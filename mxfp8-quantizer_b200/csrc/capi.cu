@@ -68,15 +68,15 @@ int current_device(DeviceState** out) {
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-// Kernel choice, shared by both quantize entries.  The pipelined kernel needs
-// 16-byte aligned Q rows and S; it reads X through one tensor map when X's
-// rows are 16-byte aligned and through one tensor map per row phase
-// (row % 8) otherwise.  Row phases are 16 * ld_x bytes apart and a tensor-map
-// stride must stay below 2^40 bytes, so larger strides of unaligned rows (only
-// reachable with sparse address reservations) take the plain-load kernel.
-bool use_pipelined(const void* x, int64_t ld_x, bool has_x, const void* q, int64_t ld_q, const void* s) {
-    const bool x_ok = (aligned(x, 16) && ld_x % 8 == 0) || ld_x < (int64_t(1) << 36);
-    return has_x && x_ok && aligned(q, 16) && ld_q % 16 == 0 && aligned(s, 16);
+// Kernel choice, shared by both quantize entries.  The pipelined kernel takes
+// every non-empty X: through one tensor map when X's rows are 16-byte aligned
+// and through one tensor map per row phase (row % 8) otherwise, and writes Q
+// and S at any offset (narrower stores where 16-byte ones cannot go).  Row
+// phases are 16 * ld_x bytes apart and a tensor-map stride must stay below
+// 2^40 bytes, so larger strides of unaligned rows (only reachable with sparse
+// address reservations) take the plain-load kernel, as does empty X.
+bool use_pipelined(const void* x, int64_t ld_x, bool has_x) {
+    return has_x && ((aligned(x, 16) && ld_x % 8 == 0) || ld_x < (int64_t(1) << 36));
 }
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -147,7 +147,7 @@ extern "C" MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int
     if (rc) return rc;
     a.status = dev->status;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return use_pipelined(x, ld_x, has_x, q, ld_q, s) ? launch_quantize_tma(a, dev->sm_count, st)
+    return use_pipelined(x, ld_x, has_x) ? launch_quantize_tma(a, dev->sm_count, st)
                                                      : launch_quantize_generic(a, dev->sm_count, st);
 }
 
@@ -200,7 +200,7 @@ extern "C" MXFP8_API int mxfp8_quantize_noalloc(const void* x, int dtype, int64_
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // Same dispatch as mxfp8_quantize; the plain-load kernel uses no scratch.
-    return use_pipelined(x, ld_x, has_x, q, ld_q, s) ? launch_quantize_tma_noalloc(a, dev, sms, st)
+    return use_pipelined(x, ld_x, has_x) ? launch_quantize_tma_noalloc(a, dev, sms, st)
                                                      : launch_quantize_generic(a, sms, st);
 }
 

@@ -1,6 +1,8 @@
-// quantize_generic.cu -- MXFP8 quantizer for layouts the pipelined kernel
-// (quantize_tma.cu) does not take: Q rows or S that are not 16-byte aligned,
-// and empty X.  Same recipe (recipe.cuh) and output contract.
+// quantize_generic.cu -- plain-load MXFP8 quantizer for what the pipelined
+// kernel (quantize_tma.cu) does not take: empty X (it then writes only the
+// padding) and X rows that are neither 16-byte aligned nor less than 2^36
+// elements apart (no tensor map can stride them).  Same recipe (recipe.cuh)
+// and output contract.
 //
 // Work item: 4 rows x one 256-column segment (8 scale blocks), one warp.
 // Lane l owns columns [8l, 8l + 8) of the segment, so a quad of lanes holds

@@ -247,7 +247,79 @@ __device__ __forceinline__ void prefetch_tile(const XMaps<ROWS>& xm, const TmaPa
     }
 }
 
-template <int DT, int STAGES, bool ROWS>
+// 16 bytes to global memory with streaming stores at a 4-byte aligned
+// address, at the widest width the address allows (8 lanes still cover 128
+// contiguous bytes per instruction).
+template <bool QU>
+__device__ __forceinline__ void store16(uint8_t* dst, const uint4& v) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(dst);
+    if (!QU || (a & 15) == 0) {
+        __stcs(reinterpret_cast<uint4*>(dst), v);
+    } else if ((a & 7) == 0) {
+        __stcs(reinterpret_cast<uint2*>(dst), make_uint2(v.x, v.y));
+        __stcs(reinterpret_cast<uint2*>(dst + 8), make_uint2(v.z, v.w));
+    } else {
+        __stcs(reinterpret_cast<unsigned int*>(dst), v.x);
+        __stcs(reinterpret_cast<unsigned int*>(dst + 4), v.y);
+        __stcs(reinterpret_cast<unsigned int*>(dst + 8), v.z);
+        __stcs(reinterpret_cast<unsigned int*>(dst + 12), v.w);
+    }
+}
+
+// QU store of one row segment of the payload tile (seg bytes, a multiple of
+// 32) from the staging row `rowbuf` (16-byte chunks XOR-swizzled by `key`) to
+// dst, which may sit at any byte offset.  A 4-byte aligned dst: lane c stores
+// its own chunk with 16/8/4-byte stores.  Otherwise the 8 lanes of the row
+// (lane c) write the aligned 16-byte chunks of the segment, one each, built
+// from 5 words read at word granularity from the staging row and
+// funnel-shifted by the remaining byte offset, so every store instruction
+// writes whole lines; the unaligned head (16 - d bytes) and tail (d bytes) go
+// out as naturally aligned 1/2/4/8-byte pieces, one per bit of their length:
+// lanes 0-3 the head's, lanes 4-7 the tail's.  No byte outside the segment is
+// written.  Measured at 8192^2 (TB/s): 8-byte aligned rows 6.5, 4-byte 5.6,
+// 1- or 2-byte 3.6 (byte-wide head/tail stores: 2.8; all-narrow stores: 1.3).
+__device__ __forceinline__ void store_row_any(uint8_t* dst, const uint8_t* rowbuf, uint32_t key, int seg, int c) {
+    const uint32_t d = (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15);
+    auto word = [&](int i) {  // word i of the segment (i < 32)
+        return *reinterpret_cast<const uint32_t*>(rowbuf + ((((uint32_t)i >> 2) ^ key) << 4) + (i & 3) * 4);
+    };
+    if ((d & 3) == 0) {  // 4-byte aligned row: each lane's own chunk, 16/8/4-byte stores
+        if (16 * c < seg) store16<true>(dst + 16 * c, *reinterpret_cast<const uint4*>(rowbuf + (((uint32_t)c ^ key) << 4)));
+        return;
+    }
+    uint8_t* base = dst - d;  // 16-byte aligned
+    if (16 * (c + 1) < seg) {
+        // aligned chunk c + 1 holds segment bytes [e, e + 16), e >= 1
+        const int e = 16 * (c + 1) - (int)d;
+        const int i0 = e >> 2;
+        const uint32_t sh = 8u * (uint32_t)(e & 3);
+        uint32_t w[5];
+#pragma unroll
+        for (int k = 0; k < 5; ++k) w[k] = word((i0 + k) & 31);  // word 32 only when sh == 0 (unused)
+        __stcs(reinterpret_cast<uint4*>(base + 16 * (c + 1)),
+               make_uint4(__funnelshift_r(w[0], w[1], sh), __funnelshift_r(w[1], w[2], sh),
+                          __funnelshift_r(w[2], w[3], sh), __funnelshift_r(w[3], w[4], sh)));
+    }
+    // piece k = c % 4 of the head (c < 4) or the tail (c >= 4), if that bit is set
+    const int k = c & 3;
+    const uint32_t h = 16 - d;
+    const bool tail = c >= 4;
+    if (((tail ? d : h) >> k) & 1u) {
+        // head pieces grow from the start, tail pieces shrink from the boundary
+        const int off = tail ? seg - (int)d + (int)(d & ~((2u << k) - 1)) : (int)(h & ((1u << k) - 1));
+        const int i = off >> 2;
+        const uint32_t sh = 8u * (uint32_t)(off & 3);
+        const uint32_t w0 = word(i), w1 = word((i + 1) & 31), w2 = word((i + 2) & 31);
+        const uint32_t lo = __funnelshift_r(w0, w1, sh), hi = __funnelshift_r(w1, w2, sh);
+        uint8_t* q = dst + off;
+        if (k == 0) __stcs(q, (unsigned char)lo);
+        else if (k == 1) __stcs(reinterpret_cast<unsigned short*>(q), (unsigned short)lo);
+        else if (k == 2) __stcs(reinterpret_cast<unsigned int*>(q), lo);
+        else __stcs(reinterpret_cast<uint2*>(q), make_uint2(lo, hi));
+    }
+}
+
+template <int DT, int STAGES, bool ROWS, bool QU>
 __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
     quantize_tma_kernel(const __grid_constant__ XMaps<ROWS> xm, const TmaParams p) {
     using L = Layout<STAGES, ROWS>;
@@ -387,15 +459,24 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
             for (int i = 0; i < 4; ++i) {
                 const int row = warp * 16 + i * 4 + (lane >> 3);
                 const int chunk = lane & 7;
-                const uint4 v = *reinterpret_cast<const uint4*>(qbuf + row * 128 + ((chunk ^ stage_key<ROWS>(row)) << 4));
                 const int grow = rt * kTileRows + row;
-                const int col = ct * kTileCols + chunk * 16;  // q_cols % 32 == 0: a chunk is all in or all out
-                if (grow < p.q_rows && col < p.q_cols)
-                    __stcs(reinterpret_cast<uint4*>(p.q + (int64_t)grow * p.ld_q + col), v);
+                if constexpr (QU) {
+                    if (grow < p.q_rows) {
+                        const int seg = p.q_cols - ct * kTileCols < kTileCols ? p.q_cols - ct * kTileCols : kTileCols;
+                        store_row_any(p.q + (int64_t)grow * p.ld_q + ct * kTileCols, qbuf + row * 128,
+                                      stage_key<ROWS>(row), seg, chunk);
+                    }
+                } else {
+                    const uint4 v =
+                        *reinterpret_cast<const uint4*>(qbuf + row * 128 + ((chunk ^ stage_key<ROWS>(row)) << 4));
+                    const int col = ct * kTileCols + chunk * 16;  // q_cols % 32 == 0: a chunk is all in or all out
+                    if (grow < p.q_rows && col < p.q_cols)
+                        __stcs(reinterpret_cast<uint4*>(p.q + (int64_t)grow * p.ld_q + col), v);
+                }
             }
             if (warp == 0) {
                 const uint4 v = *reinterpret_cast<const uint4*>(smem + L::s_off + qb * kSChunkBytes + lane * 16);
-                __stcs(reinterpret_cast<uint4*>(p.s + ((int64_t)rt * p.col_chunks + ct) * kSChunkBytes + lane * 16), v);
+                store16<QU>(p.s + ((int64_t)rt * p.col_chunks + ct) * kSChunkBytes + lane * 16, v);
             }
         }
         if (tid == 0) ctl[1] = it;
@@ -482,11 +563,11 @@ static int encode_x_maps(const QuantizeArgs& a, XMaps<ROWS>& xm) {
     }
 }
 
-template <int DT, bool ROWS>
+template <int DT, bool ROWS, bool QU>
 static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
     constexpr int kSt = ROWS ? kRowStages : kStages;
     using L = Layout<kSt, ROWS>;
-    auto kernel = quantize_tma_kernel<DT, kSt, ROWS>;
+    auto kernel = quantize_tma_kernel<DT, kSt, ROWS, QU>;
     // The shared-memory opt-in is per device: set it once per device, so that
     // later launches (including ones under stream capture) make no such call.
     static std::atomic<uint64_t> attr_set{0};
@@ -564,11 +645,21 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
 int launch_quantize_tma(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
     // rows a single tensor map can describe: 16-byte aligned base and row stride
     const bool tensor = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.ld_x % 8 == 0;
-    if (a.dtype == kBF16)
-        return tensor ? launch_tma_typed<kBF16, false>(a, sm_count, stream)
-                      : launch_tma_typed<kBF16, true>(a, sm_count, stream);
-    return tensor ? launch_tma_typed<kFP16, false>(a, sm_count, stream)
-                  : launch_tma_typed<kFP16, true>(a, sm_count, stream);
+    // outputs at any byte offset: narrower stores where a 16-byte store cannot go
+    const bool qu = (reinterpret_cast<uintptr_t>(a.q) & 15) != 0 || a.ld_q % 16 != 0 ||
+                    (reinterpret_cast<uintptr_t>(a.s) & 15) != 0;
+    if (a.dtype == kBF16) {
+        if (qu)
+            return tensor ? launch_tma_typed<kBF16, false, true>(a, sm_count, stream)
+                          : launch_tma_typed<kBF16, true, true>(a, sm_count, stream);
+        return tensor ? launch_tma_typed<kBF16, false, false>(a, sm_count, stream)
+                      : launch_tma_typed<kBF16, true, false>(a, sm_count, stream);
+    }
+    if (qu)
+        return tensor ? launch_tma_typed<kFP16, false, true>(a, sm_count, stream)
+                      : launch_tma_typed<kFP16, true, true>(a, sm_count, stream);
+    return tensor ? launch_tma_typed<kFP16, false, false>(a, sm_count, stream)
+                  : launch_tma_typed<kFP16, true, false>(a, sm_count, stream);
 }
 
 // ---------------------------------------------------------------------------

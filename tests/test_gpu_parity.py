@@ -145,8 +145,8 @@ def test_ragged_shapes_tight_geometry(m, k, capi, oracle_mod):
 
 
 @pytest.mark.parametrize("layout", ["x_ld_odd", "x_misaligned", "q_misaligned", "s_word_aligned_only",
-                                    "x_strided_tma", "q_strided"])
-def test_layouts_and_generic_path(layout, capi, oracle_mod):
+                                    "x_strided_tma", "q_strided", "q_ld_odd", "q_8_byte_offset"])
+def test_layouts(layout, capi, oracle_mod):
     bits = inputs.normal(333, 544, 5, "fp16")
     kw = {}
     if layout == "x_ld_odd":
@@ -154,14 +154,28 @@ def test_layouts_and_generic_path(layout, capi, oracle_mod):
     elif layout == "x_misaligned":
         kw = dict(x_offset=1)        # 2-byte aligned only -> row path
     elif layout == "q_misaligned":
-        kw = dict(q_offset=3)        # Q not 16-byte aligned -> plain-load kernel
+        kw = dict(q_offset=3)        # Q at an odd offset -> byte stores
     elif layout == "s_word_aligned_only":
         kw = dict(s_offset=4)
     elif layout == "x_strided_tma":
         kw = dict(ld_x=1024)         # TMA with a row stride
     elif layout == "q_strided":
         kw = dict(ld_q=800)
+    elif layout == "q_ld_odd":
+        kw = dict(ld_q=555)          # Q rows at every byte alignment
+    elif layout == "q_8_byte_offset":
+        kw = dict(q_offset=8, s_offset=12)
     check_against_oracle(capi, oracle_mod, bits, "fp16", 336, 544, **kw)
+
+
+@pytest.mark.parametrize("m,k,q_rows,q_cols", [(0, 0, 100, 64), (5, 0, 8, 32), (0, 7, 129, 32), (3, 0, 3, 4096)])
+def test_empty_x_writes_padding(m, k, q_rows, q_cols, capi, oracle_mod):
+    """Empty X (the plain-load kernel): every Q byte 0, scale 127 inside the
+    geometry and 0 beyond it, as the reference's zero-padded launch gives."""
+    bits = np.zeros((m, k), dtype=np.uint16)
+    q, s = check_against_oracle(capi, oracle_mod, bits, "bf16", q_rows, q_cols)
+    assert not q.any()
+    assert set(np.unique(s)) <= {0, 127}
 
 
 def test_padded_entry_point_matches_general(capi, oracle_mod):
@@ -389,11 +403,11 @@ def test_e2e_suite_all_configs(capi):
 
 @pytest.mark.parametrize("m,k,x_offset,dtype", [(1000, 4097, 0, "bf16"), (333, 4064, 1, "bf16"), (129, 8191, 3, "fp16"),
                                                 (64, 31, 1, "fp16"), (1, 1, 1, "bf16"), (260, 300, 0, "bf16")])
-@pytest.mark.parametrize("q_offset", [0, 8])
+@pytest.mark.parametrize("q_offset", [0, 8, 3])
 def test_odd_layouts_special_values(m, k, x_offset, dtype, q_offset, capi, oracle_mod):
-    """Odd K and 2-byte aligned X: with 16-byte aligned Q they go through the
-    pipelined kernel's row path, with Q 8 bytes off through the plain-load
-    kernel.  Special values, both geometries."""
+    """Odd K and 2-byte aligned X (the pipelined kernel's row path), with Q
+    16-byte aligned, 8 bytes off (8-byte stores) or 3 bytes off (realigned
+    line stores).  Special values, both geometries."""
     kk = (k + 31) // 32 * 32
     bits = inputs.special_values_bf16(m, kk, seed=k)[:, :k].copy() if dtype == "bf16" else \
         inputs.normal(m, k, k, "fp16", sigma=30.0)
@@ -450,12 +464,12 @@ def test_launch_count_matches_bench_accounting(m, k, capi):
     assert launches == bench.launches_per_call(m, k, k)
 
 
-def test_three_kernels_agree_across_launch_split(capi):
+def test_three_paths_agree_across_launch_split(capi):
     """38000 x 8191 bf16 (622 MB): the same X through the row path (row
     stride 8191, three launches of 148 + 148 + 1 row tiles), the tensor path
-    (row stride 8192, two launches of 296 + 1 row tiles) and the plain-load
-    kernel (Q 8 bytes off 16-byte alignment) gives identical Q and S bytes,
-    in the reference geometry."""
+    (row stride 8192, two launches of 296 + 1 row tiles) and the tensor path
+    with Q 8 bytes off 16-byte alignment (narrower stores) gives identical Q
+    and S bytes, in the reference geometry."""
     m, k = 38000, 8191
     q_rows, q_cols = (m + 7) // 8 * 8, (k + 255) // 256 * 256
     s_bytes = capi.scale_storage_bytes(q_rows, q_cols)
@@ -500,6 +514,23 @@ def test_randomized_unaligned_x(capi, oracle_mod):
             check_against_oracle(capi, oracle_mod, bits, dtype, ld_x=ld, x_offset=x_offset)
         else:
             check_against_oracle(capi, oracle_mod, bits, dtype, m, (k + 31) // 32 * 32, ld_x=ld, x_offset=x_offset)
+
+
+def test_randomized_output_layouts(capi, oracle_mod):
+    """60 seeded random cases of Q at any byte offset and row stride and S
+    at any 4-byte offset, over aligned and unaligned X."""
+    rng = np.random.default_rng(4242)
+    for case in range(60):
+        m = int(rng.integers(1, 300))
+        k = int(rng.integers(1, 1100))
+        dtype = "bf16" if rng.random() < 0.5 else "fp16"
+        q_cols = (k + 31) // 32 * 32
+        kw = dict(q_offset=int(rng.integers(0, 16)), ld_q=q_cols + int(rng.integers(0, 24)),
+                  s_offset=4 * int(rng.integers(0, 4)))
+        if rng.random() < 0.5:
+            kw.update(ld_x=k + int(rng.integers(0, 9)), x_offset=int(rng.integers(0, 8)))
+        bits = inputs.normal(m, k, 5000 + case, dtype, sigma=float(10 ** rng.uniform(-2, 2)))
+        check_against_oracle(capi, oracle_mod, bits, dtype, m, q_cols, **kw)
 
 
 def test_randomized_shapes_layouts_and_values(capi, oracle_mod):
