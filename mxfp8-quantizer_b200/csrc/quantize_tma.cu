@@ -2,7 +2,8 @@
 //
 // Work unit ("tile"): 128 rows x 128 columns of X, i.e. exactly one 512-byte
 // chunk of the packed scale layout (128 rows x 4 scale columns).  One CTA per
-// SM walks tiles round-robin.  Warp 8 (one elected lane) streams X tiles into
+// SM (two on the row path below) walks tiles round-robin.  Warp 8 (one
+// elected lane) streams X tiles into
 // a 3-deep shared-memory ring with 2-D TMA loads (two 64-column boxes,
 // 128-byte swizzle, zero fill outside (m, k)); warps 0-7 compute into one of
 // two staging buffers (payload tile + 512-byte scale chunk); one reduction
@@ -44,7 +45,12 @@
 // (272-byte rows, no swizzle) at column ct * 128, an aligned coordinate.
 // Every byte a box reads lies in the 16-byte chunks that hold the row's own
 // elements; columns past k + d_f and rows past the phase's last are zero
-// filled.  Consumers shift their 64 elements down by d_f in registers.
+// filled.  Consumers shift their 64 elements down by d_f in registers; the
+// thread map changes so that each compute warp holds one phase (tile_row).
+//
+// Outputs at any offset (template flag QU, when Q, ld_q or S is not 16-byte
+// aligned): the store pass writes Q rows through store_row_any and the scale
+// chunk with 16/8/4-byte stores (S is at least 4-byte aligned).
 //
 // Reference behaviour restated (not its structure): MXFP8_quantizer.py:355-525.
 #include <cuda.h>
@@ -276,8 +282,9 @@ __device__ __forceinline__ void store16(uint8_t* dst, const uint4& v) {
 // writes whole lines; the unaligned head (16 - d bytes) and tail (d bytes) go
 // out as naturally aligned 1/2/4/8-byte pieces, one per bit of their length:
 // lanes 0-3 the head's, lanes 4-7 the tail's.  No byte outside the segment is
-// written.  Measured at 8192^2 (TB/s): 8-byte aligned rows 6.5, 4-byte 5.6,
-// 1- or 2-byte 3.6 (byte-wide head/tail stores: 2.8; all-narrow stores: 1.3).
+// written.  Measured at 8192^2 (TB/s): 8- or 4-byte aligned rows 5.5-5.9, 1-
+// or 2-byte 3.2-3.6 (byte-wide head/tail stores: 2.8; 1-byte stores at each
+// chunk's own address: 1.3).
 __device__ __forceinline__ void store_row_any(uint8_t* dst, const uint8_t* rowbuf, uint32_t key, int seg, int c) {
     const uint32_t d = (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15);
     auto word = [&](int i) {  // word i of the segment (i < 32)
