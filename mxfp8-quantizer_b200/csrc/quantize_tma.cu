@@ -275,23 +275,24 @@ __device__ __forceinline__ void store16(uint8_t* dst, const uint4& v) {
 // QU store of one row segment of the payload tile (seg bytes, a multiple of
 // 32) from the staging row `rowbuf` (16-byte chunks XOR-swizzled by `key`) to
 // dst, which may sit at any byte offset.  A 4-byte aligned dst: lane c stores
-// its own chunk with 16/8/4-byte stores.  Otherwise the 8 lanes of the row
+// its own chunk v with 16/8/4-byte stores.  Otherwise the 8 lanes of the row
 // (lane c) write the aligned 16-byte chunks of the segment, one each, built
 // from 5 words read at word granularity from the staging row and
 // funnel-shifted by the remaining byte offset, so every store instruction
 // writes whole lines; the unaligned head (16 - d bytes) and tail (d bytes) go
 // out as naturally aligned 1/2/4/8-byte pieces, one per bit of their length:
 // lanes 0-3 the head's, lanes 4-7 the tail's.  No byte outside the segment is
-// written.  Measured at 8192^2 (TB/s): 8- or 4-byte aligned rows 5.5-5.9, 1-
-// or 2-byte 3.2-3.6 (byte-wide head/tail stores: 2.8; 1-byte stores at each
+// written.  Measured at 8192^2 (TB/s): 8- or 4-byte aligned rows 5.6-6.1, 1-
+// or 2-byte 3.3-3.7 (byte-wide head/tail stores: 2.8; 1-byte stores at each
 // chunk's own address: 1.3).
-__device__ __forceinline__ void store_row_any(uint8_t* dst, const uint8_t* rowbuf, uint32_t key, int seg, int c) {
+__device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, const uint8_t* rowbuf, uint32_t key, int seg,
+                                              int c) {
     const uint32_t d = (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15);
     auto word = [&](int i) {  // word i of the segment (i < 32)
         return *reinterpret_cast<const uint32_t*>(rowbuf + ((((uint32_t)i >> 2) ^ key) << 4) + (i & 3) * 4);
     };
-    if ((d & 3) == 0) {  // 4-byte aligned row: each lane's own chunk, 16/8/4-byte stores
-        if (16 * c < seg) store16<true>(dst + 16 * c, *reinterpret_cast<const uint4*>(rowbuf + (((uint32_t)c ^ key) << 4)));
+    if ((d & 3) == 0) {  // 4-byte aligned row: each lane's own chunk v, 16/8/4-byte stores
+        if (16 * c < seg) store16<true>(dst + 16 * c, v);
         return;
     }
     uint8_t* base = dst - d;  // 16-byte aligned
@@ -467,15 +468,15 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
                 const int row = warp * 16 + i * 4 + (lane >> 3);
                 const int chunk = lane & 7;
                 const int grow = rt * kTileRows + row;
+                // loaded before any branch, so the loads of all 4 iterations can be in flight together
+                const uint4 v = *reinterpret_cast<const uint4*>(qbuf + row * 128 + ((chunk ^ stage_key<ROWS>(row)) << 4));
                 if constexpr (QU) {
                     if (grow < p.q_rows) {
                         const int seg = p.q_cols - ct * kTileCols < kTileCols ? p.q_cols - ct * kTileCols : kTileCols;
-                        store_row_any(p.q + (int64_t)grow * p.ld_q + ct * kTileCols, qbuf + row * 128,
+                        store_row_any(p.q + (int64_t)grow * p.ld_q + ct * kTileCols, v, qbuf + row * 128,
                                       stage_key<ROWS>(row), seg, chunk);
                     }
                 } else {
-                    const uint4 v =
-                        *reinterpret_cast<const uint4*>(qbuf + row * 128 + ((chunk ^ stage_key<ROWS>(row)) << 4));
                     const int col = ct * kTileCols + chunk * 16;  // q_cols % 32 == 0: a chunk is all in or all out
                     if (grow < p.q_rows && col < p.q_cols)
                         __stcs(reinterpret_cast<uint4*>(p.q + (int64_t)grow * p.ld_q + col), v);
