@@ -402,7 +402,7 @@ def main() -> None:
                     help="directory holding the reference's MXFP8_quantizer.py (reference-kernel arm)")
     ap.add_argument("--m", type=int, default=M_DEFAULT)
     ap.add_argument("--k", type=int, default=K_DEFAULT)
-    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["c2", "c5"], default="c2",
                     help="c2: 8192x8192 per rank (weak scaling, the driver's line); "
