@@ -129,7 +129,9 @@ MXFP8_API int mxfp8_dequantize(const void* q, int64_t rows, int64_t cols, int64_
 /* Sticky device-side error word of the current device (0 = none).  Kernels
  * never trap: a pipeline wait that exceeds its time limit (about 1 s) sets a
  * bit here and the kernel returns early.  Bits: 1 = payload tile wait,
- * 2 = stage-release wait, 4 = drain wait on exit, 8 = the self-test's wait.  Reading synchronises the
+ * 2 = stage-release wait, 4 = drain wait on exit, 8 = the self-test's wait,
+ * 16 = a store outside its output was skipped (only the checked build,
+ * include/mxfp8_checked.h, tests stores).  Reading synchronises the
  * device; clear != 0 resets the word.  The word lives in a small device
  * buffer allocated on the first quantize call on each device.
  * No counterpart in the reference (its kernel waits without a limit). */

@@ -16,6 +16,7 @@ import threading
 
 PKG_DIR = pathlib.Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libmxfp8.so"
+CHECKED_LIB_PATH = PKG_DIR / "libmxfp8_checked.so"
 
 BF16, FP16, F32 = 0, 1, 2
 
@@ -50,6 +51,35 @@ class ExtensionMissing(RuntimeError):
     pass
 
 
+def configure(L: ctypes.CDLL) -> ctypes.CDLL:
+    """Declare the C ABI's argument and result types on a loaded library."""
+    i64, i32, vp = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+    L.mxfp8_scale_storage_bytes.argtypes = [i64, i64]
+    L.mxfp8_scale_storage_bytes.restype = i64
+    L.mxfp8_launch_shape.argtypes = [i64, i64, ctypes.POINTER(i64), ctypes.POINTER(i64)]
+    L.mxfp8_launch_shape.restype = i32
+    L.mxfp8_quantize.argtypes = [vp, i32, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp]
+    L.mxfp8_quantize.restype = i32
+    L.mxfp8_quantize_noalloc.argtypes = [vp, i32, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp]
+    L.mxfp8_quantize_noalloc.restype = i32
+    L.mxfp8_quantize_padded.argtypes = [vp, vp, vp, i64, i64, i64, i32, vp]
+    L.mxfp8_quantize_padded.restype = i32
+    L.mxfp8_dequantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, i64, vp]
+    L.mxfp8_dequantize.restype = i32
+    L.mxfp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]
+    L.mxfp8_device_status.restype = i32
+    L.mxfp8_selftest_bounded_wait.argtypes = [ctypes.c_uint32, vp]
+    L.mxfp8_selftest_bounded_wait.restype = i32
+    L.mxfp8_strerror.argtypes = [i32]
+    L.mxfp8_strerror.restype = ctypes.c_char_p
+    L.mxfp8_last_error.argtypes = []
+    L.mxfp8_last_error.restype = ctypes.c_char_p
+    if hasattr(L, "mxfp8_checked_window_slack"):
+        L.mxfp8_checked_window_slack.argtypes = [i64]
+        L.mxfp8_checked_window_slack.restype = i32
+    return L
+
+
 def lib() -> ctypes.CDLL:
     """Load libmxfp8.so once; raise if it has not been built."""
     global _lib
@@ -61,30 +91,16 @@ def lib() -> ctypes.CDLL:
         if not LIB_PATH.exists():
             raise ExtensionMissing(
                 f"{LIB_PATH} is not built; run `python {PKG_DIR.name}/build.py` (or __graft_entry__.build())")
-        L = ctypes.CDLL(str(LIB_PATH))
-        i64, i32, vp = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
-        L.mxfp8_scale_storage_bytes.argtypes = [i64, i64]
-        L.mxfp8_scale_storage_bytes.restype = i64
-        L.mxfp8_launch_shape.argtypes = [i64, i64, ctypes.POINTER(i64), ctypes.POINTER(i64)]
-        L.mxfp8_launch_shape.restype = i32
-        L.mxfp8_quantize.argtypes = [vp, i32, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp]
-        L.mxfp8_quantize.restype = i32
-        L.mxfp8_quantize_noalloc.argtypes = [vp, i32, i64, i64, i64, vp, i64, i64, i64, vp, i64, vp]
-        L.mxfp8_quantize_noalloc.restype = i32
-        L.mxfp8_quantize_padded.argtypes = [vp, vp, vp, i64, i64, i64, i32, vp]
-        L.mxfp8_quantize_padded.restype = i32
-        L.mxfp8_dequantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, i64, vp]
-        L.mxfp8_dequantize.restype = i32
-        L.mxfp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]
-        L.mxfp8_device_status.restype = i32
-        L.mxfp8_selftest_bounded_wait.argtypes = [ctypes.c_uint32, vp]
-        L.mxfp8_selftest_bounded_wait.restype = i32
-        L.mxfp8_strerror.argtypes = [i32]
-        L.mxfp8_strerror.restype = ctypes.c_char_p
-        L.mxfp8_last_error.argtypes = []
-        L.mxfp8_last_error.restype = ctypes.c_char_p
-        _lib = L
-        return L
+        _lib = configure(ctypes.CDLL(str(LIB_PATH)))
+        return _lib
+
+
+def checked_lib() -> ctypes.CDLL:
+    """libmxfp8_checked.so (include/mxfp8_checked.h): the same C ABI with every
+    global store tested against its output; for tests, not for production."""
+    if not CHECKED_LIB_PATH.exists():
+        raise ExtensionMissing(f"{CHECKED_LIB_PATH} is not built; run `python {PKG_DIR.name}/build.py`")
+    return configure(ctypes.CDLL(str(CHECKED_LIB_PATH)))
 
 
 def strerror(code: int) -> str:

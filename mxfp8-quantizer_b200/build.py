@@ -1,9 +1,11 @@
-"""Build libmxfp8.so (sm_100a) in-tree with nvcc.
+"""Build libmxfp8.so and libmxfp8_checked.so (sm_100a) in-tree with nvcc.
 
     python mxfp8-quantizer_b200/build.py [--force] [--ptxas-verbose]
 
 The library links the CUDA runtime statically and exports only the C ABI
-of include/mxfp8.h.  nvcc cross-compiles, so this runs without a GPU.
+of include/mxfp8.h.  The checked build compiles the same sources with
+MXFP8_CHECKED (every global store tested against its output's bytes; see
+include/mxfp8_checked.h).  nvcc cross-compiles, so this runs without a GPU.
 """
 
 from __future__ import annotations
@@ -19,8 +21,9 @@ PKG = pathlib.Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libmxfp8.so"
+CHECKED_LIB = PKG / "libmxfp8_checked.so"
 SOURCES = ["capi.cu", "quantize_tma.cu", "quantize_generic.cu", "dequantize.cu", "selftest.cu"]
-HEADERS = ["ptx.cuh", "recipe.cuh", "launch.h"]
+HEADERS = ["ptx.cuh", "recipe.cuh", "launch.h", "guard.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -32,33 +35,48 @@ def nvcc() -> str:
 
 
 def inputs() -> list[pathlib.Path]:
-    return [CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS] + [ROOT / "include" / "mxfp8.h",
-                                                                        pathlib.Path(__file__)]
+    return [CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS] + [
+        ROOT / "include" / "mxfp8.h", ROOT / "include" / "mxfp8_checked.h", pathlib.Path(__file__)]
 
 
-def up_to_date() -> bool:
-    if not LIB.exists():
+def up_to_date(lib: pathlib.Path) -> bool:
+    if not lib.exists():
         return False
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     return all(p.stat().st_mtime <= t for p in inputs())
 
 
-def build(force: bool = False, verbose_ptxas: bool = False) -> pathlib.Path:
-    if not force and up_to_date():
-        return LIB
-    tmp = LIB.with_name(f".libmxfp8.{os.getpid()}.so")
+def _command(out: pathlib.Path, checked: bool, verbose_ptxas: bool) -> list[str]:
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-           "-Xcompiler", "-Wall", "-I", str(ROOT / "include"), "-o", str(tmp)]
+           "-Xcompiler", "-Wall", "-I", str(ROOT / "include"), "-o", str(out)]
+    if checked:
+        cmd.append("-DMXFP8_CHECKED")
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
-    cmd += [str(CSRC / s) for s in SOURCES]
-    proc = subprocess.run(cmd, capture_output=True, text=True)
-    if proc.returncode != 0:
-        sys.stderr.write(proc.stdout + proc.stderr)
-        raise RuntimeError("nvcc failed building libmxfp8.so")
-    if verbose_ptxas:
-        sys.stderr.write(proc.stderr)
-    os.replace(tmp, LIB)
+    return cmd + [str(CSRC / s) for s in SOURCES]
+
+
+def build(force: bool = False, verbose_ptxas: bool = False) -> pathlib.Path:
+    """Build both libraries (in parallel) if a source is newer; returns the product library."""
+    jobs = []
+    for lib, checked in ((LIB, False), (CHECKED_LIB, True)):
+        if force or not up_to_date(lib):
+            tmp = lib.with_name(f".{lib.stem}.{os.getpid()}.so")
+            proc = subprocess.Popen(_command(tmp, checked, verbose_ptxas and not checked), stdout=subprocess.PIPE,
+                                    stderr=subprocess.PIPE, text=True)
+            jobs.append((lib, tmp, proc))
+    failed = []
+    for lib, tmp, proc in jobs:
+        out, err = proc.communicate()
+        if proc.returncode != 0:
+            sys.stderr.write(out + err)
+            failed.append(lib.name)
+            continue
+        if verbose_ptxas:
+            sys.stderr.write(err)
+        os.replace(tmp, lib)
+    if failed:
+        raise RuntimeError(f"nvcc failed building {', '.join(failed)}")
     return LIB
 
 

@@ -2,10 +2,14 @@
 // include/mxfp8.h): argument validation, per-device state, kernel choice.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
 #include "../../include/mxfp8.h"
+#ifdef MXFP8_CHECKED
+#include "../../include/mxfp8_checked.h"
+#endif
 #include "launch.h"
 
 namespace mxfp8 {
@@ -81,6 +85,22 @@ bool use_pipelined(const void* x, int64_t ld_x, bool has_x) {
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+#ifdef MXFP8_CHECKED
+std::atomic<int64_t> g_window_slack{0};
+#endif
+
+// The bytes [base, base + bytes) a kernel may write.  The checked build
+// narrows it by mxfp8_checked_window_slack bytes, to show that its store
+// guards fire; the product build ignores the window.
+StoreWindow make_window(void* base, int64_t bytes) {
+    uint8_t* lo = static_cast<uint8_t*>(base);
+#ifdef MXFP8_CHECKED
+    bytes -= g_window_slack.load(std::memory_order_relaxed);
+    if (bytes < 0) bytes = 0;
+#endif
+    return StoreWindow{lo, lo + bytes};
+}
+
 }  // namespace
 
 void set_last_error(const char* what, int code) {
@@ -140,6 +160,8 @@ extern "C" MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int
     a.scale_rows = ceil_div(q_rows, 128) * 128;
     a.scale_cols = q_cols / 32;
     a.col_chunks = ceil_div(a.scale_cols, 4);
+    a.qw = make_window(q, (q_rows - 1) * ld_q + q_cols);
+    a.sw = make_window(s, mxfp8_scale_storage_bytes(q_rows, q_cols));
     if ((a.scale_rows / 128) * a.col_chunks > kInt32Max) return MXFP8_ERR_SHAPE;
 
     DeviceState* dev = nullptr;
@@ -182,6 +204,8 @@ extern "C" MXFP8_API int mxfp8_quantize_noalloc(const void* x, int dtype, int64_
     a.scale_rows = ceil_div(q_rows, 128) * 128;
     a.scale_cols = q_cols / 32;
     a.col_chunks = ceil_div(a.scale_cols, 4);
+    a.qw = make_window(q, (q_rows - 1) * ld_q + q_cols);
+    a.sw = make_window(s, mxfp8_scale_storage_bytes(q_rows, q_cols));
     a.status = nullptr;
     if ((a.scale_rows / 128) * a.col_chunks > kInt32Max) return MXFP8_ERR_SHAPE;
 
@@ -221,8 +245,9 @@ extern "C" MXFP8_API int mxfp8_dequantize(const void* q, int64_t rows, int64_t c
     DeviceState* dev = nullptr;
     int rc = current_device(&dev);
     if (rc) return rc;
+    const StoreWindow ow = make_window(out, ((rows - 1) * ld_out + cols) * (out_dtype == MXFP8_F32 ? 4 : 2));
     return launch_dequantize(static_cast<const uint8_t*>(q), rows, cols, ld_q, static_cast<const uint8_t*>(s), out,
-                             out_dtype, ld_out, static_cast<cudaStream_t>(stream));
+                             out_dtype, ld_out, ow, dev->status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" MXFP8_API int mxfp8_device_status(uint32_t* status_out, int clear) {
@@ -248,6 +273,14 @@ extern "C" MXFP8_API int mxfp8_selftest_bounded_wait(uint32_t limit_us, mxfp8_st
     if (rc) return rc;
     return launch_bounded_wait_selftest(dev->status, limit_us, static_cast<cudaStream_t>(stream));
 }
+
+#ifdef MXFP8_CHECKED
+extern "C" MXFP8_API int mxfp8_checked_window_slack(int64_t bytes) {
+    if (bytes < 0 || bytes > (int64_t(1) << 20)) return MXFP8_ERR_SHAPE;
+    g_window_slack.store(bytes, std::memory_order_relaxed);
+    return MXFP8_OK;
+}
+#endif
 
 extern "C" MXFP8_API const char* mxfp8_strerror(int status) {
     switch (status) {

@@ -32,38 +32,40 @@ __device__ __forceinline__ float ue8m0_to_float(uint32_t b) {
 
 // 16 decoded values -> out (16 contiguous elements at element index o).
 template <int OUT>
-__device__ __forceinline__ void store16(void* out, int64_t o, const float (&v)[16], bool vec) {
+__device__ __forceinline__ void store16(void* out, int64_t o, const float (&v)[16], bool vec, const StoreWindow& w,
+                                        unsigned int* status) {
     if constexpr (OUT == MXFP8_F32) {
         float* p = static_cast<float*>(out) + o;
         if (vec) {
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                __stcs(reinterpret_cast<float4*>(p) + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+                gstore(reinterpret_cast<float4*>(p) + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]),
+                       w, status);
         } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) p[i] = v[i];
+            for (int i = 0; i < 16; ++i) gstore(p + i, v[i], w, status);
         }
     } else {
-        uint32_t w[8];
+        uint32_t h[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if constexpr (OUT == MXFP8_BF16) {
-                const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-                w[i] = *reinterpret_cast<const uint32_t*>(&h);
+                const __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+                h[i] = *reinterpret_cast<const uint32_t*>(&t);
             } else {
-                const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-                w[i] = *reinterpret_cast<const uint32_t*>(&h);
+                const __half2 t = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+                h[i] = *reinterpret_cast<const uint32_t*>(&t);
             }
         }
-        uint16_t* p = static_cast<uint16_t*>(out) + o;
+        unsigned short* p = static_cast<unsigned short*>(out) + o;
         if (vec) {
-            __stcs(reinterpret_cast<uint4*>(p), make_uint4(w[0], w[1], w[2], w[3]));
-            __stcs(reinterpret_cast<uint4*>(p) + 1, make_uint4(w[4], w[5], w[6], w[7]));
+            gstore(reinterpret_cast<uint4*>(p), make_uint4(h[0], h[1], h[2], h[3]), w, status);
+            gstore(reinterpret_cast<uint4*>(p) + 1, make_uint4(h[4], h[5], h[6], h[7]), w, status);
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                p[2 * i] = (uint16_t)(w[i] & 0xFFFFu);
-                p[2 * i + 1] = (uint16_t)(w[i] >> 16);
+                gstore(p + 2 * i, (unsigned short)(h[i] & 0xFFFFu), w, status);
+                gstore(p + 2 * i + 1, (unsigned short)(h[i] >> 16), w, status);
             }
         }
     }
@@ -93,7 +95,7 @@ constexpr int kMaxCtasPerSm = 64;
 template <int OUT>
 __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restrict__ q, int64_t rows, int64_t cols,
                                                          int64_t ld_q, const uint8_t* __restrict__ s, void* out,
-                                                         int64_t ld_out) {
+                                                         int64_t ld_out, StoreWindow ow, unsigned int* status) {
     // Programmatic dependent launch: start early, touch memory only after
     // the previous kernel in the stream has completed.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -134,13 +136,13 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint8_t* __restri
             decode16<OUT>(w[j], ue8m0_to_float(sb[j]), v);
             const int64_t o = r * ld_out + hp * 16;
             const bool vec = ((reinterpret_cast<uintptr_t>(out) + (uint64_t)o * kOutBytes) & 15) == 0;
-            store16<OUT>(out, o, v, vec);
+            store16<OUT>(out, o, v, vec, ow, status);
         }
     }
 }
 
 int launch_dequantize(const uint8_t* q, int64_t rows, int64_t cols, int64_t ld_q, const uint8_t* s, void* out,
-                      int out_dtype, int64_t ld_out, cudaStream_t stream) {
+                      int out_dtype, int64_t ld_out, StoreWindow ow, unsigned int* status, cudaStream_t stream) {
     const int64_t n = rows * (cols / 16);
     if (n == 0) return MXFP8_OK;
     int dev = 0, sms = 148;
@@ -160,13 +162,15 @@ int launch_dequantize(const uint8_t* q, int64_t rows, int64_t cols, int64_t ld_q
     cudaError_t e;
     switch (out_dtype) {
         case MXFP8_F32:
-            e = cudaLaunchKernelEx(&cfg, dequantize_kernel<MXFP8_F32>, q, rows, cols, ld_q, s, out, ld_out);
+            e = cudaLaunchKernelEx(&cfg, dequantize_kernel<MXFP8_F32>, q, rows, cols, ld_q, s, out, ld_out, ow, status);
             break;
         case MXFP8_BF16:
-            e = cudaLaunchKernelEx(&cfg, dequantize_kernel<MXFP8_BF16>, q, rows, cols, ld_q, s, out, ld_out);
+            e = cudaLaunchKernelEx(&cfg, dequantize_kernel<MXFP8_BF16>, q, rows, cols, ld_q, s, out, ld_out, ow,
+                                   status);
             break;
         default:
-            e = cudaLaunchKernelEx(&cfg, dequantize_kernel<MXFP8_FP16>, q, rows, cols, ld_q, s, out, ld_out);
+            e = cudaLaunchKernelEx(&cfg, dequantize_kernel<MXFP8_FP16>, q, rows, cols, ld_q, s, out, ld_out, ow,
+                                   status);
             break;
     }
     if (e == cudaSuccess) e = cudaGetLastError();

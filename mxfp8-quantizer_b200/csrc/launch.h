@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "guard.cuh"
+
 namespace mxfp8 {
 
 // Problem description after argument validation.
@@ -18,6 +20,7 @@ struct QuantizeArgs {
     int64_t scale_cols;   // q_cols / 32
     int64_t col_chunks;   // ceil(scale_cols / 4)
     unsigned int* status; // device error word (may be null)
+    StoreWindow qw, sw;   // bytes the kernels may write: Q rows, S storage
 };
 
 // Returned by launchers: 0, or a negative mxfp8_status.
@@ -26,7 +29,8 @@ int launch_quantize_generic(const QuantizeArgs& a, int sm_count, cudaStream_t st
 // Same kernel as launch_quantize_tma, scratch in a fixed device array (never allocates).
 int launch_quantize_tma_noalloc(const QuantizeArgs& a, int dev, int sm_count, cudaStream_t stream);
 int launch_dequantize(const uint8_t* q, int64_t rows, int64_t cols, int64_t ld_q, const uint8_t* s,
-                      void* out, int out_dtype, int64_t ld_out, cudaStream_t stream);
+                      void* out, int out_dtype, int64_t ld_out, StoreWindow ow, unsigned int* status,
+                      cudaStream_t stream);
 
 int launch_bounded_wait_selftest(unsigned int* status, uint32_t limit_us, cudaStream_t stream);
 

@@ -67,7 +67,9 @@ __global__ void __launch_bounds__(256) quantize_generic_kernel(const uint16_t* _
                                                                int64_t ld_x, uint8_t* __restrict__ q,
                                                                int64_t q_rows, int64_t q_cols, int64_t ld_q,
                                                                uint8_t* __restrict__ s, int64_t scale_rows,
-                                                               int64_t scale_cols, int64_t col_chunks) {
+                                                               int64_t scale_cols, int64_t col_chunks,
+                                                               StoreWindow qw, StoreWindow sw,
+                                                               unsigned int* status) {
     const int lane = threadIdx.x & 31;
     const int64_t segs = (col_chunks + 1) / 2;               // 256-column segments
     const int64_t groups = (scale_rows + kRowsPerItem - 1) / kRowsPerItem;
@@ -97,10 +99,11 @@ __global__ void __launch_bounds__(256) quantize_generic_kernel(const uint16_t* _
             if (r < q_rows && c < q_cols) {
                 uint8_t* dst = q + r * ld_q + c;
                 if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
-                    *reinterpret_cast<uint2*>(dst) = qq;
+                    gstore(reinterpret_cast<uint2*>(dst), qq, qw, status);
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) dst[e] = (uint8_t)((e < 4 ? qq.x : qq.y) >> (8 * (e & 3)));
+                    for (int e = 0; e < 8; ++e)
+                        gstore(dst + e, (unsigned char)((e < 4 ? qq.x : qq.y) >> (8 * (e & 3))), qw, status);
                 }
             }
             const int64_t blk = seg * 8 + (lane >> 2);
@@ -110,8 +113,8 @@ __global__ void __launch_bounds__(256) quantize_generic_kernel(const uint16_t* _
             const uint32_t b2 = __shfl_down_sync(0xFFFFFFFFu, byte, 8);
             const uint32_t b3 = __shfl_down_sync(0xFFFFFFFFu, byte, 12);
             if ((lane & 15) == 0 && (blk >> 2) < col_chunks)
-                *reinterpret_cast<uint32_t*>(s + scale_offset(r, blk, col_chunks)) =
-                    byte | (b1 << 8) | (b2 << 16) | (b3 << 24);
+                gstore(reinterpret_cast<unsigned int*>(s + scale_offset(r, blk, col_chunks)),
+                       byte | (b1 << 8) | (b2 << 16) | (b3 << 24), sw, status);
         }
     }
 }
@@ -126,10 +129,12 @@ int launch_quantize_generic(const QuantizeArgs& a, int sm_count, cudaStream_t st
     const uint16_t* x = static_cast<const uint16_t*>(a.x);
     if (a.dtype == kBF16)
         quantize_generic_kernel<kBF16><<<(int)blocks, 256, 0, stream>>>(
-            x, a.m, a.k, a.ld_x, a.q, a.q_rows, a.q_cols, a.ld_q, a.s, a.scale_rows, a.scale_cols, a.col_chunks);
+            x, a.m, a.k, a.ld_x, a.q, a.q_rows, a.q_cols, a.ld_q, a.s, a.scale_rows, a.scale_cols, a.col_chunks,
+            a.qw, a.sw, a.status);
     else
         quantize_generic_kernel<kFP16><<<(int)blocks, 256, 0, stream>>>(
-            x, a.m, a.k, a.ld_x, a.q, a.q_rows, a.q_cols, a.ld_q, a.s, a.scale_rows, a.scale_cols, a.col_chunks);
+            x, a.m, a.k, a.ld_x, a.q, a.q_rows, a.q_cols, a.ld_q, a.s, a.scale_rows, a.scale_cols, a.col_chunks,
+            a.qw, a.sw, a.status);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_last_error("quantize_generic_kernel launch", (int)e);

@@ -134,6 +134,7 @@ struct TmaParams {
     int col_chunks;
     uint8_t* s;
     unsigned int* status;
+    StoreWindow qw, sw;  // what the stores may touch (checked build)
 };
 
 __device__ __forceinline__ bool bar_red_or(uint32_t id, uint32_t n, bool pred) {
@@ -257,18 +258,18 @@ __device__ __forceinline__ void prefetch_tile(const XMaps<ROWS>& xm, const TmaPa
 // address, at the widest width the address allows (8 lanes still cover 128
 // contiguous bytes per instruction).
 template <bool QU>
-__device__ __forceinline__ void store16(uint8_t* dst, const uint4& v) {
+__device__ __forceinline__ void store16(uint8_t* dst, const uint4& v, const StoreWindow& w, unsigned int* status) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(dst);
     if (!QU || (a & 15) == 0) {
-        __stcs(reinterpret_cast<uint4*>(dst), v);
+        gstore(reinterpret_cast<uint4*>(dst), v, w, status);
     } else if ((a & 7) == 0) {
-        __stcs(reinterpret_cast<uint2*>(dst), make_uint2(v.x, v.y));
-        __stcs(reinterpret_cast<uint2*>(dst + 8), make_uint2(v.z, v.w));
+        gstore(reinterpret_cast<uint2*>(dst), make_uint2(v.x, v.y), w, status);
+        gstore(reinterpret_cast<uint2*>(dst + 8), make_uint2(v.z, v.w), w, status);
     } else {
-        __stcs(reinterpret_cast<unsigned int*>(dst), v.x);
-        __stcs(reinterpret_cast<unsigned int*>(dst + 4), v.y);
-        __stcs(reinterpret_cast<unsigned int*>(dst + 8), v.z);
-        __stcs(reinterpret_cast<unsigned int*>(dst + 12), v.w);
+        gstore(reinterpret_cast<unsigned int*>(dst), v.x, w, status);
+        gstore(reinterpret_cast<unsigned int*>(dst + 4), v.y, w, status);
+        gstore(reinterpret_cast<unsigned int*>(dst + 8), v.z, w, status);
+        gstore(reinterpret_cast<unsigned int*>(dst + 12), v.w, w, status);
     }
 }
 
@@ -286,13 +287,13 @@ __device__ __forceinline__ void store16(uint8_t* dst, const uint4& v) {
 // or 2-byte 3.3-3.7 (byte-wide head/tail stores: 2.8; 1-byte stores at each
 // chunk's own address: 1.3).
 __device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, const uint8_t* rowbuf, uint32_t key, int seg,
-                                              int c) {
+                                              int c, const StoreWindow& w, unsigned int* status) {
     const uint32_t d = (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15);
     auto word = [&](int i) {  // word i of the segment (i < 32)
         return *reinterpret_cast<const uint32_t*>(rowbuf + ((((uint32_t)i >> 2) ^ key) << 4) + (i & 3) * 4);
     };
     if ((d & 3) == 0) {  // 4-byte aligned row: each lane's own chunk v, 16/8/4-byte stores
-        if (16 * c < seg) store16<true>(dst + 16 * c, v);
+        if (16 * c < seg) store16<true>(dst + 16 * c, v, w, status);
         return;
     }
     uint8_t* base = dst - d;  // 16-byte aligned
@@ -301,12 +302,13 @@ __device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, cons
         const int e = 16 * (c + 1) - (int)d;
         const int i0 = e >> 2;
         const uint32_t sh = 8u * (uint32_t)(e & 3);
-        uint32_t w[5];
+        uint32_t x[5];
 #pragma unroll
-        for (int k = 0; k < 5; ++k) w[k] = word((i0 + k) & 31);  // word 32 only when sh == 0 (unused)
-        __stcs(reinterpret_cast<uint4*>(base + 16 * (c + 1)),
-               make_uint4(__funnelshift_r(w[0], w[1], sh), __funnelshift_r(w[1], w[2], sh),
-                          __funnelshift_r(w[2], w[3], sh), __funnelshift_r(w[3], w[4], sh)));
+        for (int k = 0; k < 5; ++k) x[k] = word((i0 + k) & 31);  // word 32 only when sh == 0 (unused)
+        gstore(reinterpret_cast<uint4*>(base + 16 * (c + 1)),
+               make_uint4(__funnelshift_r(x[0], x[1], sh), __funnelshift_r(x[1], x[2], sh),
+                          __funnelshift_r(x[2], x[3], sh), __funnelshift_r(x[3], x[4], sh)),
+               w, status);
     }
     // piece k = c % 4 of the head (c < 4) or the tail (c >= 4), if that bit is set
     const int k = c & 3;
@@ -320,10 +322,10 @@ __device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, cons
         const uint32_t w0 = word(i), w1 = word((i + 1) & 31), w2 = word((i + 2) & 31);
         const uint32_t lo = __funnelshift_r(w0, w1, sh), hi = __funnelshift_r(w1, w2, sh);
         uint8_t* q = dst + off;
-        if (k == 0) __stcs(q, (unsigned char)lo);
-        else if (k == 1) __stcs(reinterpret_cast<unsigned short*>(q), (unsigned short)lo);
-        else if (k == 2) __stcs(reinterpret_cast<unsigned int*>(q), lo);
-        else __stcs(reinterpret_cast<uint2*>(q), make_uint2(lo, hi));
+        if (k == 0) gstore(q, (unsigned char)lo, w, status);
+        else if (k == 1) gstore(reinterpret_cast<unsigned short*>(q), (unsigned short)lo, w, status);
+        else if (k == 2) gstore(reinterpret_cast<unsigned int*>(q), lo, w, status);
+        else gstore(reinterpret_cast<uint2*>(q), make_uint2(lo, hi), w, status);
     }
 }
 
@@ -474,17 +476,17 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
                     if (grow < p.q_rows) {
                         const int seg = p.q_cols - ct * kTileCols < kTileCols ? p.q_cols - ct * kTileCols : kTileCols;
                         store_row_any(p.q + (int64_t)grow * p.ld_q + ct * kTileCols, v, qbuf + row * 128,
-                                      stage_key<ROWS>(row), seg, chunk);
+                                      stage_key<ROWS>(row), seg, chunk, p.qw, p.status);
                     }
                 } else {
                     const int col = ct * kTileCols + chunk * 16;  // q_cols % 32 == 0: a chunk is all in or all out
                     if (grow < p.q_rows && col < p.q_cols)
-                        __stcs(reinterpret_cast<uint4*>(p.q + (int64_t)grow * p.ld_q + col), v);
+                        gstore(reinterpret_cast<uint4*>(p.q + (int64_t)grow * p.ld_q + col), v, p.qw, p.status);
                 }
             }
             if (warp == 0) {
                 const uint4 v = *reinterpret_cast<const uint4*>(smem + L::s_off + qb * kSChunkBytes + lane * 16);
-                store16<QU>(p.s + ((int64_t)rt * p.col_chunks + ct) * kSChunkBytes + lane * 16, v);
+                store16<QU>(p.s + ((int64_t)rt * p.col_chunks + ct) * kSChunkBytes + lane * 16, v, p.sw, p.status);
             }
         }
         if (tid == 0) ctl[1] = it;
@@ -612,6 +614,8 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
     p.col_chunks = (int)a.col_chunks;
     p.s = a.s;
     p.status = a.status;
+    p.qw = a.qw;
+    p.sw = a.sw;
     // Long problems run as several launches of at most kMaxTilesPerLaunch
     // tiles (whole row tiles, i.e. contiguous slices of Q and S), chained by
     // the dependent launch.  Persistent CTAs drift apart over thousands of

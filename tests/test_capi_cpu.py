@@ -16,8 +16,8 @@ pkg = MXFP8_quantizer.load_package()
 capi = pkg._capi
 
 
-def declared_symbols():
-    text = (ROOT / "include" / "mxfp8.h").read_text()
+def declared_symbols(header="mxfp8.h"):
+    text = (ROOT / "include" / header).read_text()
     return sorted(set(re.findall(r"MXFP8_API\s+[\w\s\*]+?\b(mxfp8_\w+)\s*\(", text)))
 
 
@@ -29,6 +29,18 @@ def test_library_exports_every_declared_symbol():
     lib = capi.lib()
     for name in declared_symbols():
         assert hasattr(lib, name), name
+
+
+def test_checked_library_exports_both_headers():
+    """libmxfp8_checked.so: the whole C ABI plus the checked-build hook, which
+    the product library does not carry."""
+    checked = capi.checked_lib()
+    for name in declared_symbols() + declared_symbols("mxfp8_checked.h"):
+        assert hasattr(checked, name), name
+    assert declared_symbols("mxfp8_checked.h") == ["mxfp8_checked_window_slack"]
+    assert not hasattr(capi.lib(), "mxfp8_checked_window_slack")
+    assert checked.mxfp8_checked_window_slack(-1) == capi.ERR_SHAPE
+    assert checked.mxfp8_checked_window_slack(0) == capi.OK
 
 
 def test_library_is_sm100a_only():
