@@ -550,12 +550,36 @@ static int encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t
     return MXFP8_OK;
 }
 
+#ifdef MXFP8_CHECKED
+// Checked build: the bytes a 2-D map can read, [base, base + (rows - 1) *
+// stride + 2 * cols), must lie in the 16-byte chunks that hold X's own
+// elements (from X's first chunk to the end of the chunk holding its last
+// element).  Bounds of whole rows only; the row path's per-row spans are
+// checked by construction (each map row starts in its own row's first chunk).
+static int check_map_extent(const QuantizeArgs& a, uintptr_t base, uint64_t cols, uint64_t rows, uint64_t stride) {
+    const uintptr_t x = reinterpret_cast<uintptr_t>(a.x);
+    const uintptr_t lo = x & ~(uintptr_t)15;
+    const uintptr_t hi = (x + 2 * (uintptr_t)((a.m - 1) * a.ld_x + a.k) + 15) & ~(uintptr_t)15;
+    const uintptr_t end = base + (rows - 1) * stride + 2 * cols;
+    if (base < lo || end > hi) {
+        set_last_error("checked build: a tensor map of X reaches outside X's bytes", 0);
+        return MXFP8_ERR_TENSOR_MAP;
+    }
+    return MXFP8_OK;
+}
+#endif
+
 // Tensor maps of X.  Tensor path: one map, 64 x 128 boxes, 128-byte swizzle.
 // Row path: one map per phase f < min(m, 8) (see the file comment).
 template <bool ROWS>
 static int encode_x_maps(const QuantizeArgs& a, XMaps<ROWS>& xm) {
     memset(&xm, 0, sizeof(xm));
     if constexpr (!ROWS) {
+#ifdef MXFP8_CHECKED
+        if (int rc = check_map_extent(a, reinterpret_cast<uintptr_t>(a.x), (uint64_t)a.k, (uint64_t)a.m,
+                                      (uint64_t)a.ld_x * 2))
+            return rc;
+#endif
         return encode_2d(&xm.map[0], a.x, (uint64_t)a.k, (uint64_t)a.m, (uint64_t)a.ld_x * 2, kBoxCols, kTileRows,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
@@ -565,6 +589,9 @@ static int encode_x_maps(const QuantizeArgs& a, XMaps<ROWS>& xm) {
             const uintptr_t base = row0 & ~(uintptr_t)15;
             const uint64_t d = (row0 - base) / 2;  // elements of misalignment, < 8
             const uint64_t rows = (uint64_t)((a.m - f + kPhases - 1) / kPhases);
+#ifdef MXFP8_CHECKED
+            if (int rc = check_map_extent(a, base, (uint64_t)a.k + d, rows, (uint64_t)a.ld_x * 2 * kPhases)) return rc;
+#endif
             int rc = encode_2d(&xm.map[f], reinterpret_cast<const void*>(base), (uint64_t)a.k + d, rows,
                                (uint64_t)a.ld_x * 2 * kPhases, kRowBoxCols, kPhaseRows, CU_TENSOR_MAP_SWIZZLE_NONE);
             if (rc) return rc;
