@@ -273,7 +273,8 @@ def dequantize_arm(args, pkg, capi, xs, qs, ss, launch, n_ws, m, k, s_bytes, str
     ys = [torch.empty((m, k), dtype=torch.bfloat16, device=xs[0].device) for _ in range(n_ws)]
     lib = capi.lib()
     sh = stream.cuda_stream
-    args_d = [(qs[i].data_ptr(), m, k, k, ss[i].data_ptr(), ys[i].data_ptr(), capi.BF16, k, sh) for i in range(n_ws)]
+    args_d = [(qs[i].data_ptr(), m, k, k, ss[i].data_ptr(), s_bytes, ys[i].data_ptr(), capi.BF16, k, sh)
+              for i in range(n_ws)]
 
     def deq(i):
         rc = lib.mxfp8_dequantize(*args_d[i])

@@ -118,13 +118,14 @@ MXFP8_API int mxfp8_quantize_noalloc(const void* x, int dtype, int64_t m, int64_
 MXFP8_API int mxfp8_quantize_padded(const void* x, void* q_dwords, void* s_words, int64_t m, int64_t k,
                           int64_t s_word_count, int dtype, mxfp8_stream_t stream);
 
-/* Dequantize Q (rows, cols) with packed scales S into out (rows, cols) of
- * out_dtype (MXFP8_BF16, MXFP8_FP16 or MXFP8_F32), row stride ld_out
- * elements: out = e4m3(Q) * 2^(S - 127); scale byte 255 decodes to NaN.
- * cols % 32 == 0.  The inverse used by the reference's end-to-end check,
- * MXFP8_quantizer.py:1179-1187. */
+/* Dequantize Q (rows, cols) with packed scales S (s_bytes >=
+ * mxfp8_scale_storage_bytes(rows, cols), else MXFP8_ERR_SCALE_BUFFER) into
+ * out (rows, cols) of out_dtype (MXFP8_BF16, MXFP8_FP16 or MXFP8_F32), row
+ * stride ld_out elements: out = e4m3(Q) * 2^(S - 127); scale byte 255 decodes
+ * to NaN.  cols % 32 == 0.  The inverse used by the reference's end-to-end
+ * check, MXFP8_quantizer.py:1179-1187. */
 MXFP8_API int mxfp8_dequantize(const void* q, int64_t rows, int64_t cols, int64_t ld_q, const void* s,
-                     void* out, int out_dtype, int64_t ld_out, mxfp8_stream_t stream);
+                               int64_t s_bytes, void* out, int out_dtype, int64_t ld_out, mxfp8_stream_t stream);
 
 /* Sticky device-side error word of the current device (0 = none).  Kernels
  * never trap: a pipeline wait that exceeds its time limit (about 1 s) sets a

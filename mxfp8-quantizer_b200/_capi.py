@@ -64,7 +64,7 @@ def configure(L: ctypes.CDLL) -> ctypes.CDLL:
     L.mxfp8_quantize_noalloc.restype = i32
     L.mxfp8_quantize_padded.argtypes = [vp, vp, vp, i64, i64, i64, i32, vp]
     L.mxfp8_quantize_padded.restype = i32
-    L.mxfp8_dequantize.argtypes = [vp, i64, i64, i64, vp, vp, i32, i64, vp]
+    L.mxfp8_dequantize.argtypes = [vp, i64, i64, i64, vp, i64, vp, i32, i64, vp]
     L.mxfp8_dequantize.restype = i32
     L.mxfp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]
     L.mxfp8_device_status.restype = i32
@@ -155,10 +155,10 @@ def quantize_padded(x_ptr: int, q_ptr: int, s_ptr: int, m: int, k: int, s_word_c
     check(rc, "quantizer launch")
 
 
-def dequantize(q_ptr: int, rows: int, cols: int, ld_q: int, s_ptr: int, out_ptr: int, out_dtype: int,
-               ld_out: int, stream: int) -> None:
-    rc = lib().mxfp8_dequantize(q_ptr or None, rows, cols, ld_q, s_ptr or None, out_ptr or None, out_dtype,
-                                ld_out, stream or None)
+def dequantize(q_ptr: int, rows: int, cols: int, ld_q: int, s_ptr: int, s_bytes: int, out_ptr: int,
+               out_dtype: int, ld_out: int, stream: int) -> None:
+    rc = lib().mxfp8_dequantize(q_ptr or None, rows, cols, ld_q, s_ptr or None, s_bytes, out_ptr or None,
+                                out_dtype, ld_out, stream or None)
     check(rc, "dequantizer launch")
 
 

@@ -235,12 +235,16 @@ extern "C" MXFP8_API int mxfp8_quantize_padded(const void* x, void* q_dwords, vo
     return mxfp8_quantize(x, dtype, m, k, k, q_dwords, m, k, k, s_words, s_word_count * 4, stream);
 }
 
-extern "C" MXFP8_API int mxfp8_dequantize(const void* q, int64_t rows, int64_t cols, int64_t ld_q, const void* s, void* out,
-                                int out_dtype, int64_t ld_out, mxfp8_stream_t stream) {
+extern "C" MXFP8_API int mxfp8_dequantize(const void* q, int64_t rows, int64_t cols, int64_t ld_q, const void* s,
+                                          int64_t s_bytes, void* out, int out_dtype, int64_t ld_out,
+                                          mxfp8_stream_t stream) {
     if (out_dtype != MXFP8_BF16 && out_dtype != MXFP8_FP16 && out_dtype != MXFP8_F32) return MXFP8_ERR_DTYPE;
-    if (rows < 0 || cols < 0 || cols % 32 != 0 || ld_q < cols || ld_out < cols) return MXFP8_ERR_SHAPE;
+    if (rows < 0 || cols < 0 || cols % 32 != 0 || ld_q < cols || ld_out < cols || rows > kInt32Max ||
+        cols > kInt32Max)
+        return MXFP8_ERR_SHAPE;
     if (rows == 0 || cols == 0) return MXFP8_OK;
     if (!q || !s || !out) return MXFP8_ERR_NULL_POINTER;
+    if (s_bytes < mxfp8_scale_storage_bytes(rows, cols)) return MXFP8_ERR_SCALE_BUFFER;
     if (!aligned(out, out_dtype == MXFP8_F32 ? 4 : 2)) return MXFP8_ERR_ALIGNMENT;
     DeviceState* dev = nullptr;
     int rc = current_device(&dev);

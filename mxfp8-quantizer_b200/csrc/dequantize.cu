@@ -43,7 +43,7 @@ __device__ __forceinline__ void store16(void* out, int64_t o, const float (&v)[1
                        w, status);
         } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) gstore(p + i, v[i], w, status);
+            for (int i = 0; i < 16; ++i) gstore_plain(p + i, v[i], w, status);
         }
     } else {
         uint32_t h[8];
@@ -64,8 +64,8 @@ __device__ __forceinline__ void store16(void* out, int64_t o, const float (&v)[1
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                gstore(p + 2 * i, (unsigned short)(h[i] & 0xFFFFu), w, status);
-                gstore(p + 2 * i + 1, (unsigned short)(h[i] >> 16), w, status);
+                gstore_plain(p + 2 * i, (unsigned short)(h[i] & 0xFFFFu), w, status);
+                gstore_plain(p + 2 * i + 1, (unsigned short)(h[i] >> 16), w, status);
             }
         }
     }

@@ -99,11 +99,11 @@ __global__ void __launch_bounds__(256) quantize_generic_kernel(const uint16_t* _
             if (r < q_rows && c < q_cols) {
                 uint8_t* dst = q + r * ld_q + c;
                 if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
-                    gstore(reinterpret_cast<uint2*>(dst), qq, qw, status);
+                    gstore_plain(reinterpret_cast<uint2*>(dst), qq, qw, status);
                 } else {
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
-                        gstore(dst + e, (unsigned char)((e < 4 ? qq.x : qq.y) >> (8 * (e & 3))), qw, status);
+                        gstore_plain(dst + e, (unsigned char)((e < 4 ? qq.x : qq.y) >> (8 * (e & 3))), qw, status);
                 }
             }
             const int64_t blk = seg * 8 + (lane >> 2);
@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(256) quantize_generic_kernel(const uint16_t* _
             const uint32_t b2 = __shfl_down_sync(0xFFFFFFFFu, byte, 8);
             const uint32_t b3 = __shfl_down_sync(0xFFFFFFFFu, byte, 12);
             if ((lane & 15) == 0 && (blk >> 2) < col_chunks)
-                gstore(reinterpret_cast<unsigned int*>(s + scale_offset(r, blk, col_chunks)),
+                gstore_plain(reinterpret_cast<unsigned int*>(s + scale_offset(r, blk, col_chunks)),
                        byte | (b1 << 8) | (b2 << 16) | (b3 << 24), sw, status);
         }
     }

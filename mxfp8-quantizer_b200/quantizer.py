@@ -172,6 +172,8 @@ def quantize(x: torch.Tensor, q: torch.Tensor | None = None, s: torch.Tensor | N
     ``q_rows``/``q_cols`` default to the reference's padded launch shape.
     Pass ``q_rows=m, q_cols=ceil(k/32)*32`` for the tight layout (padding
     scale bytes 0).  Preallocated ``q``/``s`` are written in place."""
+    if not x.is_cuda:
+        raise ValueError("x must be a CUDA tensor")
     x = _as_row_major(x)
     m, k = x.shape
     if q_rows is None or q_cols is None:
@@ -182,8 +184,6 @@ def quantize(x: torch.Tensor, q: torch.Tensor | None = None, s: torch.Tensor | N
         q = torch.empty((q_rows, q_cols), dtype=torch.float8_e4m3fn, device=x.device)
     if s is None:
         s = torch.empty((_capi.scale_storage_bytes(q_rows, q_cols),), dtype=torch.uint8, device=x.device)
-    if not x.is_cuda:
-        raise ValueError("x must be a CUDA tensor")
     if (q.dim() != 2 or q.element_size() != 1 or q.shape[0] < q_rows or q.shape[1] < q_cols
             or q.stride(1) != 1 or q.device != x.device):
         raise ValueError("q must be a row-major (>= q_rows, >= q_cols) one-byte matrix on x's device")
@@ -199,6 +199,8 @@ def dequantize(q: torch.Tensor, s: torch.Tensor, out_dtype: torch.dtype = torch.
     """E4M3 payload + packed UE8M0 scales -> out_dtype (bf16, fp16 or fp32)."""
     if q.dim() != 2 or q.element_size() != 1 or q.stride(1) != 1 or not q.is_cuda:
         raise ValueError("q must be a row-major one-byte CUDA matrix")
+    if s.device != q.device or not s.is_contiguous():
+        raise ValueError("s must be a contiguous buffer on q's device")
     rows, cols = q.shape
     codes = {torch.float32: _capi.F32, torch.bfloat16: _capi.BF16, torch.float16: _capi.FP16}
     if out_dtype not in codes:
@@ -206,8 +208,8 @@ def dequantize(q: torch.Tensor, s: torch.Tensor, out_dtype: torch.dtype = torch.
     code = codes[out_dtype]
     out = torch.empty((rows, cols), dtype=out_dtype, device=q.device)
     with torch.cuda.device(q.device):
-        _capi.dequantize(q.data_ptr(), rows, cols, q.stride(0), s.data_ptr(), out.data_ptr(), code, out.stride(0),
-                         _stream_handle(stream))
+        _capi.dequantize(q.data_ptr(), rows, cols, q.stride(0), s.data_ptr(), s.numel() * s.element_size(),
+                         out.data_ptr(), code, out.stride(0), _stream_handle(stream))
     return out
 
 

@@ -102,10 +102,13 @@ def test_padded_entry_rejects_unpadded_shapes():
 
 
 def test_dequantize_rejects_bad_arguments():
+    ok_s = capi.scale_storage_bytes(4, 32)
     with pytest.raises(ValueError):
-        capi.dequantize(0x1000, 4, 33, 33, 0x2000, 0x3000, 2, 33, 0)
+        capi.dequantize(0x1000, 4, 33, 33, 0x2000, ok_s, 0x3000, 2, 33, 0)    # cols % 32
     with pytest.raises(ValueError):
-        capi.dequantize(0x1000, 4, 32, 32, 0x2000, 0x3000, 9, 32, 0)
+        capi.dequantize(0x1000, 4, 32, 32, 0x2000, ok_s, 0x3000, 9, 32, 0)    # dtype
+    with pytest.raises(ValueError, match="scale buffer"):
+        capi.dequantize(0x1000, 4, 32, 32, 0x2000, ok_s - 1, 0x3000, 2, 32, 0)  # S too small
 
 
 def test_strerror_names_every_code():

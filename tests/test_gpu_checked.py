@@ -96,7 +96,7 @@ def test_checked_build_dequantize(out_dtype, ld_out, libs):
     outs = []
     for L in (prod, checked):
         out = torch.full((m * ld_out * esize + 64,), CANARY, dtype=torch.uint8, device="cuda")
-        rc = L.mxfp8_dequantize(q.data_ptr(), m, k, k, s.data_ptr(), out.data_ptr(), out_dtype, ld_out,
+        rc = L.mxfp8_dequantize(q.data_ptr(), m, k, k, s.data_ptr(), s_bytes, out.data_ptr(), out_dtype, ld_out,
                                 torch.cuda.current_stream().cuda_stream)
         assert rc == 0
         torch.cuda.synchronize()

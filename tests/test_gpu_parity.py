@@ -357,7 +357,7 @@ def test_dequantize_unaligned_output_rows(capi, oracle_mod):
     s = torch.from_numpy(s_ref).cuda()
     ld = k + 1
     out = torch.full((m * ld + 8,), float("nan"), dtype=torch.float32, device="cuda")
-    capi.dequantize(q.data_ptr(), m, k, k, s.data_ptr(), out.data_ptr() + 4, capi.F32, ld,
+    capi.dequantize(q.data_ptr(), m, k, k, s.data_ptr(), s.numel(), out.data_ptr() + 4, capi.F32, ld,
                     torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     got = out[1:1 + m * ld].view(m, ld)[:, :k].cpu().numpy()
