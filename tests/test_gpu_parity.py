@@ -364,31 +364,37 @@ def test_dequantize_unaligned_output_rows(capi, oracle_mod):
     np.testing.assert_array_equal(got, oracle_mod.dequantize(q_ref, s_ref))
 
 
-def test_quantize_inside_cuda_graph(capi, oracle_mod):
+@pytest.mark.parametrize("layout", ["tensor", "unaligned_rows", "q_any_offset"])
+def test_quantize_inside_cuda_graph(layout, capi, oracle_mod):
     """Launches captured in a CUDA graph (dependent-launch edges between them)
-    replay bit-exactly; inputs are refreshed in place between replays."""
-    m, k = 1024, 2048
+    replay bit-exactly; inputs are refreshed in place between replays.  Every
+    kernel variant: one tensor map, per-row-phase maps, any-offset stores."""
+    m = 1024
+    k = 2047 if layout == "unaligned_rows" else 2048
+    q_cols, q_off = 2048, (3 if layout == "q_any_offset" else 0)
     srcs = [inputs.normal(m, k, 700 + i) for i in range(3)]
-    sb = capi.scale_storage_bytes(m, k)
+    sb = capi.scale_storage_bytes(m, q_cols)
     x = torch.empty((m, k), dtype=torch.int16, device="cuda")
-    q = torch.empty((3, m, k), dtype=torch.uint8, device="cuda")
+    q = torch.empty((3, m * q_cols + 64), dtype=torch.uint8, device="cuda")
     s = torch.empty((3, sb), dtype=torch.uint8, device="cuda")
     x.copy_(torch.from_numpy(srcs[0].view(np.int16)))
-    capi.quantize(x.data_ptr(), 0, m, k, k, q[0].data_ptr(), m, k, k, s[0].data_ptr(), sb,
+    capi.quantize(x.data_ptr(), 0, m, k, k, q[0].data_ptr() + q_off, m, q_cols, q_cols, s[0].data_ptr(), sb,
                   torch.cuda.current_stream().cuda_stream)      # first call outside capture
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         st = torch.cuda.current_stream().cuda_stream
         for i in range(3):
-            capi.quantize(x.data_ptr(), 0, m, k, k, q[i].data_ptr(), m, k, k, s[i].data_ptr(), sb, st)
+            capi.quantize(x.data_ptr(), 0, m, k, k, q[i].data_ptr() + q_off, m, q_cols, q_cols, s[i].data_ptr(),
+                          sb, st)
     for src in srcs:
         x.copy_(torch.from_numpy(src.view(np.int16)))
         g.replay()
         torch.cuda.synchronize()
-        q_ref, s_ref = oracle_mod.quantize(src, "bf16", m, k)
+        q_ref, s_ref = oracle_mod.quantize(src, "bf16", m, q_cols)
         for i in range(3):
-            assert np.array_equal(q[i].cpu().numpy(), q_ref)
+            got = q[i].cpu().numpy()[q_off:q_off + m * q_cols].reshape(m, q_cols)
+            assert np.array_equal(got, q_ref)
             assert np.array_equal(s[i].cpu().numpy(), s_ref)
     del g
 
