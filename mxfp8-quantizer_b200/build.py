@@ -23,7 +23,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libmxfp8.so"
 CHECKED_LIB = PKG / "libmxfp8_checked.so"
 SOURCES = ["capi.cu", "quantize_tma.cu", "quantize_generic.cu", "dequantize.cu", "selftest.cu"]
-HEADERS = ["ptx.cuh", "recipe.cuh", "launch.h", "guard.cuh"]
+HEADERS = ["ptx.cuh", "recipe.cuh", "launch.h", "guard.cuh", "tile.cuh", "row_path.cuh", "stores.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -65,77 +65,11 @@
 #include "launch.h"
 #include "ptx.cuh"
 #include "recipe.cuh"
+#include "row_path.cuh"
+#include "stores.cuh"
+#include "tile.cuh"
 
 namespace mxfp8 {
-
-constexpr int kTileRows = 128;
-constexpr int kTileCols = 128;
-constexpr int kBoxCols = 64;                              // 64 x 16 bit = 128 B swizzle span
-constexpr int kStageBytes = kTileRows * kTileCols * 2;    // 32 KiB of X per tile
-constexpr int kBoxBytes = kStageBytes / 2;
-constexpr int kQTileBytes = kTileRows * kTileCols;        // 16 KiB of payload per tile
-constexpr int kSChunkBytes = 512;
-constexpr int kComputeWarps = 8;
-constexpr int kComputeThreads = kComputeWarps * 32;
-constexpr int kThreads = kComputeThreads + 32;            // + producer warp
-constexpr int kQBufs = 2;
-constexpr int kPrefetchTiles = 2;                        // L2 prefetch before the dependency wait
-constexpr uint64_t kWaitLimitNs = 1000000000ull;          // 1 s per pipeline wait
-constexpr uint32_t kBarCompute = 1;                       // named barrier id
-
-constexpr unsigned kErrTileWait = 1u, kErrReleaseWait = 2u, kErrDrainWait = 4u;
-
-// Row path staging: per phase, a 16-row box of 136 columns (272 bytes: 128
-// columns plus up to 7 of misalignment, a multiple of 16 bytes).
-constexpr int kPhases = 8;
-constexpr int kPhaseRows = kTileRows / kPhases;           // 16 box rows per phase and tile
-constexpr int kRowBoxCols = 136;
-constexpr int kRowSlot = kRowBoxCols * 2;                 // 272
-constexpr int kPhaseBoxBytes = kPhaseRows * kRowSlot;     // 4352 (a multiple of 128)
-constexpr int kRowStageBytes = kPhases * kPhaseBoxBytes;  // 34 KiB of X per tile
-// The row path's compute warps do more work per tile (the register shift), so
-// it runs 2 CTAs per SM with 2 stages each (~105 KiB of shared memory apiece)
-// for twice the warps: 8192 x 8191 bf16 6.25 vs 5.99 TB/s with 1 CTA x 3
-// stages (1 CTA x 4 or x 2 stages: slower still).
-constexpr int kRowStages = 2;
-constexpr int kRowCtasPerSm = 2;
-
-template <bool ROWS>
-struct XMaps {
-    CUtensorMap map[ROWS ? kPhases : 1];
-};
-
-template <int STAGES, bool ROWS>
-struct Layout {
-    static constexpr int stage_bytes = ROWS ? kRowStageBytes : kStageBytes;
-    static constexpr int x_off = 0;
-    static constexpr int q_off = STAGES * stage_bytes;
-    static constexpr int s_off = q_off + kQBufs * kQTileBytes;
-    static constexpr int bar_off = s_off + kQBufs * kSChunkBytes;
-    static constexpr int ctl_off = bar_off + 2 * STAGES * 8;
-    static constexpr int bytes = ctl_off + 16;
-    static constexpr int alloc = bytes + 1024;  // slack to align the base to 1024
-};
-
-struct TmaParams {
-    int rt_offset;  // first row tile of this launch (long problems are split by row tiles)
-    const uint8_t* x;  // row path only: X base and row stride (for each row's misalignment)
-    int64_t ld_x;
-    int m;
-    int k;
-    int n_phases;   // row path: tensor maps in use, min(m, 8)
-    uint8_t* q;
-    int64_t ld_q;
-    int q_rows;
-    int q_cols;
-    int n_tiles;
-    int n_col_tiles;
-    int scale_cols;
-    int col_chunks;
-    uint8_t* s;
-    unsigned int* status;
-    StoreWindow qw, sw;  // what the stores may touch (checked build)
-};
 
 __device__ __forceinline__ bool bar_red_or(uint32_t id, uint32_t n, bool pred) {
     uint32_t r;
@@ -152,81 +86,6 @@ __device__ __forceinline__ bool bar_red_or(uint32_t id, uint32_t n, bool pred) {
 
 __device__ __forceinline__ void report(unsigned int* status, unsigned code) {
     if (status) atomicOr(status, code);
-}
-
-// Row of the tile that compute thread `tid` handles, and which 64 of its 128
-// columns (h).  Tensor path: row tid % 128, h = tid / 128.  Row path: warp w
-// takes the 16 rows 8j + w of tensor-map phase w, lane l row j = l % 16 and
-// h = l / 16, so a warp shares one misalignment (warp-uniform re-align code)
-// and the 8 lanes of a shared-memory phase read 8 consecutive box rows of
-// 272 bytes, which start in 8 different 16-byte bank groups: conflict-free.
-template <bool ROWS>
-__device__ __forceinline__ int tile_row(int tid) {
-    return ROWS ? (tid & 15) * kPhases + (tid >> 5) : (tid & (kTileRows - 1));
-}
-template <bool ROWS>
-__device__ __forceinline__ int tile_half(int tid) {
-    return ROWS ? (tid >> 4) & 1 : tid >> 7;
-}
-
-// XOR key of the payload staging buffer's 128-byte swizzle for tile row r:
-// distinct across the 8 rows that one 8-lane phase writes.
-template <bool ROWS>
-__device__ __forceinline__ uint32_t stage_key(int r) {
-    return ROWS ? (uint32_t)((r >> 3) & 7) : (uint32_t)(r & 7);
-}
-
-// Words W .. W+32 of v, shifted down by a further 2 bytes when sel says so.
-template <int W>
-__device__ __forceinline__ void shift_words(const uint32_t (&v)[36], uint32_t sel, uint32_t (&w0)[16],
-                                            uint32_t (&w1)[16]) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const uint32_t x = __byte_perm(v[W + i], v[W + i + 1], sel);
-        if (i < 16) w0[i] = x; else w1[i - 16] = x;
-    }
-}
-
-// Row path: this thread's 64 elements (columns c0 + 64h ..) of row `row` from
-// its 272-byte box row, re-aligned to 16-bit lanes and zeroed outside (m, k).
-// Column c0 sits `off` bytes into the box row (off < 16, even, the same for
-// the whole warp).  The thread loads the 9 aligned 16-byte words from byte
-// 128h on, then takes 32 words from word off / 4 on, each a byte permute of
-// two neighbours (a 2-byte shift when off % 4 == 2).  Warp-uniform branches
-// pick the word offset, so no per-word selects are needed.
-__device__ __forceinline__ void read_row_words(const TmaParams& p, const uint8_t* slot, int row, int c0, int h,
-                                               uint32_t (&w0)[16], uint32_t (&w1)[16]) {
-    const int cf = c0 + 64 * h;
-    if (row >= p.m || cf >= p.k) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w0[i] = w1[i] = 0u;
-        return;
-    }
-    // low 4 bits of X's address of (row, c0): 32-bit arithmetic suffices
-    const uint32_t off = ((uint32_t)reinterpret_cast<uintptr_t>(p.x) +
-                          2u * ((uint32_t)row * (uint32_t)p.ld_x + (uint32_t)c0)) & 15u;
-    uint32_t v[36];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) {
-        const uint4 t = *reinterpret_cast<const uint4*>(slot + 128 * h + 16 * i);
-        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
-    }
-    const uint32_t sel = (off & 2u) ? 0x5432u : 0x3210u;
-    switch (off >> 2) {
-        case 0: shift_words<0>(v, sel, w0, w1); break;
-        case 1: shift_words<1>(v, sel, w0, w1); break;
-        case 2: shift_words<2>(v, sel, w0, w1); break;
-        default: shift_words<3>(v, sel, w0, w1); break;
-    }
-    if (cf + 64 > p.k) {  // the columns cross K (the same for the whole warp)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int c = cf + 2 * i;
-            uint32_t& x = i < 16 ? w0[i] : w1[i - 16];
-            if (c >= p.k) x = 0u;
-            else if (c + 1 >= p.k) x &= 0xFFFFu;
-        }
-    }
 }
 
 // Issue the TMA loads of tile (rt, ct) into the stage at shared address dst.
@@ -251,81 +110,6 @@ __device__ __forceinline__ void prefetch_tile(const XMaps<ROWS>& xm, const TmaPa
     } else {
         tma_prefetch_l2_2d(&xm.map[0], ct * kTileCols, rt * kTileRows);
         tma_prefetch_l2_2d(&xm.map[0], ct * kTileCols + kBoxCols, rt * kTileRows);
-    }
-}
-
-// 16 bytes to global memory with streaming stores at a 4-byte aligned
-// address, at the widest width the address allows (8 lanes still cover 128
-// contiguous bytes per instruction).
-template <bool QU>
-__device__ __forceinline__ void store16(uint8_t* dst, const uint4& v, const StoreWindow& w, unsigned int* status) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(dst);
-    if (!QU || (a & 15) == 0) {
-        gstore(reinterpret_cast<uint4*>(dst), v, w, status);
-    } else if ((a & 7) == 0) {
-        gstore(reinterpret_cast<uint2*>(dst), make_uint2(v.x, v.y), w, status);
-        gstore(reinterpret_cast<uint2*>(dst + 8), make_uint2(v.z, v.w), w, status);
-    } else {
-        gstore(reinterpret_cast<unsigned int*>(dst), v.x, w, status);
-        gstore(reinterpret_cast<unsigned int*>(dst + 4), v.y, w, status);
-        gstore(reinterpret_cast<unsigned int*>(dst + 8), v.z, w, status);
-        gstore(reinterpret_cast<unsigned int*>(dst + 12), v.w, w, status);
-    }
-}
-
-// QU store of one row segment of the payload tile (seg bytes, a multiple of
-// 32) from the staging row `rowbuf` (16-byte chunks XOR-swizzled by `key`) to
-// dst, which may sit at any byte offset.  A 4-byte aligned dst: lane c stores
-// its own chunk v with 16/8/4-byte stores.  Otherwise the 8 lanes of the row
-// (lane c) write the aligned 16-byte chunks of the segment, one each, built
-// from 5 words read at word granularity from the staging row and
-// funnel-shifted by the remaining byte offset, so every store instruction
-// writes whole lines; the unaligned head (16 - d bytes) and tail (d bytes) go
-// out as naturally aligned 1/2/4/8-byte pieces, one per bit of their length:
-// lanes 0-3 the head's, lanes 4-7 the tail's.  No byte outside the segment is
-// written.  Measured at 8192^2 (TB/s): 8- or 4-byte aligned rows 5.6-6.1, 1-
-// or 2-byte 3.3-3.7 (byte-wide head/tail stores: 2.8; 1-byte stores at each
-// chunk's own address: 1.3).
-__device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, const uint8_t* rowbuf, uint32_t key, int seg,
-                                              int c, const StoreWindow& w, unsigned int* status) {
-    const uint32_t d = (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15);
-    auto word = [&](int i) {  // word i of the segment (i < 32)
-        return *reinterpret_cast<const uint32_t*>(rowbuf + ((((uint32_t)i >> 2) ^ key) << 4) + (i & 3) * 4);
-    };
-    if ((d & 3) == 0) {  // 4-byte aligned row: each lane's own chunk v, 16/8/4-byte stores
-        if (16 * c < seg) store16<true>(dst + 16 * c, v, w, status);
-        return;
-    }
-    uint8_t* base = dst - d;  // 16-byte aligned
-    if (16 * (c + 1) < seg) {
-        // aligned chunk c + 1 holds segment bytes [e, e + 16), e >= 1
-        const int e = 16 * (c + 1) - (int)d;
-        const int i0 = e >> 2;
-        const uint32_t sh = 8u * (uint32_t)(e & 3);
-        uint32_t x[5];
-#pragma unroll
-        for (int k = 0; k < 5; ++k) x[k] = word((i0 + k) & 31);  // word 32 only when sh == 0 (unused)
-        gstore(reinterpret_cast<uint4*>(base + 16 * (c + 1)),
-               make_uint4(__funnelshift_r(x[0], x[1], sh), __funnelshift_r(x[1], x[2], sh),
-                          __funnelshift_r(x[2], x[3], sh), __funnelshift_r(x[3], x[4], sh)),
-               w, status);
-    }
-    // piece k = c % 4 of the head (c < 4) or the tail (c >= 4), if that bit is set
-    const int k = c & 3;
-    const uint32_t h = 16 - d;
-    const bool tail = c >= 4;
-    if (((tail ? d : h) >> k) & 1u) {
-        // head pieces grow from the start, tail pieces shrink from the boundary
-        const int off = tail ? seg - (int)d + (int)(d & ~((2u << k) - 1)) : (int)(h & ((1u << k) - 1));
-        const int i = off >> 2;
-        const uint32_t sh = 8u * (uint32_t)(off & 3);
-        const uint32_t w0 = word(i), w1 = word((i + 1) & 31), w2 = word((i + 2) & 31);
-        const uint32_t lo = __funnelshift_r(w0, w1, sh), hi = __funnelshift_r(w1, w2, sh);
-        uint8_t* q = dst + off;
-        if (k == 0) gstore(q, (unsigned char)lo, w, status);
-        else if (k == 1) gstore(reinterpret_cast<unsigned short*>(q), (unsigned short)lo, w, status);
-        else if (k == 2) gstore(reinterpret_cast<unsigned int*>(q), lo, w, status);
-        else gstore(reinterpret_cast<uint2*>(q), make_uint2(lo, hi), w, status);
     }
 }
 
