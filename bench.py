@@ -161,6 +161,7 @@ def base_line(args, world: int) -> dict:
             "workload": f"{args.m}x{args.k} bf16 -> e4m3 + ue8m0 (tcgen05 128x4 chunks) per rank; "
                         f"rank r owns rows [r*{args.m}, (r+1)*{args.m}) of a ({args.m}*N)x{args.k} matrix",
             "m_per_rank": args.m, "k": args.k, "input_dtype": "bf16", "global_m": args.m * world,
+            "q_offset_bytes": args.q_offset,
             "parallelism": f"row shards of 128-row chunks x{world}, no collective",
         },
     }
@@ -410,10 +411,14 @@ def main() -> None:
                          "c5: the 131072x16384 N(0,2) matrix split by 128-row chunks over the ranks (strong scaling)")
     ap.add_argument("--op", choices=["quantize", "dequantize"], default="quantize",
                     help="dequantize: time mxfp8_dequantize (E4M3 + scales -> bf16) on the same workload")
+    ap.add_argument("--q-offset", type=int, default=0,
+                    help="place each Q this many bytes past a 16-byte boundary (the kernel's any-offset store path)")
     ap.add_argument("--profile", action="store_true",
                     help="kernel launches only (verify, warm-up, K launches): the command profiled with ncu")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if not 0 <= args.q_offset < 64:
+        raise SystemExit("--q-offset must be in [0, 64)")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -462,7 +467,9 @@ def main() -> None:
     n_ws = max(2, math.ceil(3 * l2 / ws_bytes))
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     xs = [torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16) for _ in range(n_ws)]
-    qs = [torch.empty((m, q_cols), dtype=torch.uint8, device=dev) for _ in range(n_ws)]
+    # Q as a view args.q_offset bytes into a slightly larger buffer (0: 16-byte aligned)
+    qs = [torch.empty((m * q_cols + 64,), dtype=torch.uint8, device=dev)[args.q_offset:args.q_offset + m * q_cols]
+          .view(m, q_cols) for _ in range(n_ws)]
     ss = [torch.empty((s_bytes,), dtype=torch.uint8, device=dev) for _ in range(n_ws)]
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
