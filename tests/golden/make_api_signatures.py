@@ -34,8 +34,37 @@ def api_signatures(path: pathlib.Path) -> dict:
     return {"functions": funcs, "constants": consts}
 
 
+RETURNING = ("run_quantizer", "prepare_and_quantize", "run_e2e_verification", "run_e2e_suite",
+             "verify_quantizer_outputs", "materialize_quantizer_buffers")
+
+
+def return_keys(path: pathlib.Path) -> dict:
+    """Keys of the dict each function in RETURNING returns, wherever it is
+    defined (the reference defines them inside build_runtime): a dict literal
+    in the return statement, or the literal assigned to the returned name."""
+    tree = ast.parse(path.read_text())
+    out = {}
+    for fn in ast.walk(tree):
+        if not (isinstance(fn, ast.FunctionDef) and fn.name in RETURNING):
+            continue
+        literals = {}
+        for node in ast.walk(fn):
+            if isinstance(node, ast.Assign) and isinstance(node.value, ast.Dict):
+                for t in node.targets:
+                    if isinstance(t, ast.Name):
+                        literals[t.id] = node.value
+        for node in ast.walk(fn):
+            if isinstance(node, ast.Return) and node.value is not None:
+                d = node.value if isinstance(node.value, ast.Dict) else (
+                    literals.get(node.value.id) if isinstance(node.value, ast.Name) else None)
+                if d is not None:
+                    out[fn.name] = sorted(k.value for k in d.keys if isinstance(k, ast.Constant))
+    return out
+
+
 def main() -> None:
     out = api_signatures(pathlib.Path(sys.argv[1]) / "MXFP8_quantizer.py")
+    out["return_keys"] = return_keys(pathlib.Path(sys.argv[1]) / "MXFP8_quantizer.py")
     (HERE / "api_signatures.json").write_text(json.dumps(out, indent=1, sort_keys=True) + "\n")
     print(json.dumps(out, indent=1, sort_keys=True))
 

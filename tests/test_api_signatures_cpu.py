@@ -33,3 +33,13 @@ def test_function_signature_matches(name):
         except ValueError:                       # a module-level name, e.g. DEFAULT_ROWS_PER_CTA
             expect = getattr(MXFP8_quantizer, text)
         assert ours == expect, (name, param, ours, expect)
+
+
+@pytest.mark.parametrize("name", sorted(GOLDEN["return_keys"]))
+def test_returned_dict_keys_match(name):
+    """The dict each entry point returns has the reference's keys (read from
+    this repository's source the same way the fixture was read)."""
+    from make_api_signatures import return_keys
+
+    ours = return_keys(ROOT / "mxfp8-quantizer_b200" / "quantizer.py")
+    assert ours.get(name) == GOLDEN["return_keys"][name]
