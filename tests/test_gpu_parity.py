@@ -258,6 +258,15 @@ def test_drop_in_api_small(capi):
     pkg = MXFP8_quantizer.load_package()
     dense = pkg.decode_scale_bytes(torch.from_numpy(s), 1024, 4096).numpy()
     assert (dense[:1000, 127] == 127).all() and (dense[1000:] == 0).all()
+    # the returned dicts carry exactly the reference's keys at run time too
+    import json
+    import pathlib
+
+    keys = json.loads((pathlib.Path(__file__).parent / "golden" / "api_signatures.json").read_text())["return_keys"]
+    assert sorted(r) == keys["run_quantizer"]
+    assert sorted(res) == keys["prepare_and_quantize"]
+    assert sorted(res["buffers"]) == keys["materialize_quantizer_buffers"]
+    assert sorted(res["verify"]) == keys["verify_quantizer_outputs"]
 
 
 def test_cold_l2_benchmark_mode(capi):
@@ -405,6 +414,12 @@ def test_e2e_suite_all_configs(capi):
     r = MXFP8_quantizer.run_e2e_suite()
     assert r["e2e_suite_passed"] and r["num_configs"] == 6
     assert all(c["quantizer_verify_passed"] and c["max_err_ratio"] < 1.0 for c in r["configs"])
+    import json
+    import pathlib
+
+    keys = json.loads((pathlib.Path(__file__).parent / "golden" / "api_signatures.json").read_text())["return_keys"]
+    assert sorted(r) == keys["run_e2e_suite"]
+    assert sorted(MXFP8_quantizer.run_e2e_verification()) == keys["run_e2e_verification"]
 
 
 @pytest.mark.parametrize("m,k,x_offset,dtype", [(1000, 4097, 0, "bf16"), (333, 4064, 1, "bf16"), (129, 8191, 3, "fp16"),
