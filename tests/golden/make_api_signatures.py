@@ -35,7 +35,18 @@ def api_signatures(path: pathlib.Path) -> dict:
 
 
 RETURNING = ("run_quantizer", "prepare_and_quantize", "run_e2e_verification", "run_e2e_suite",
-             "verify_quantizer_outputs", "materialize_quantizer_buffers")
+             "verify_quantizer_outputs", "materialize_quantizer_buffers", "benchmark_compiled_quantizer",
+             "build_runtime")
+
+
+def own_nodes(fn: ast.FunctionDef):
+    """The nodes of a function's body, not descending into nested functions."""
+    stack = list(fn.body)
+    while stack:
+        node = stack.pop()
+        yield node
+        if not isinstance(node, (ast.FunctionDef, ast.AsyncFunctionDef, ast.Lambda)):
+            stack.extend(ast.iter_child_nodes(node))
 
 
 def return_keys(path: pathlib.Path) -> dict:
@@ -48,12 +59,12 @@ def return_keys(path: pathlib.Path) -> dict:
         if not (isinstance(fn, ast.FunctionDef) and fn.name in RETURNING):
             continue
         literals = {}
-        for node in ast.walk(fn):
+        for node in own_nodes(fn):
             if isinstance(node, ast.Assign) and isinstance(node.value, ast.Dict):
                 for t in node.targets:
                     if isinstance(t, ast.Name):
                         literals[t.id] = node.value
-        for node in ast.walk(fn):
+        for node in own_nodes(fn):
             if isinstance(node, ast.Return) and node.value is not None:
                 d = node.value if isinstance(node.value, ast.Dict) else (
                     literals.get(node.value.id) if isinstance(node.value, ast.Name) else None)
