@@ -27,8 +27,8 @@ SUMMARY_KEYS = (
 
 def main() -> None:
     ap = argparse.ArgumentParser(description="Benchmark the MXFP8 quantizer kernel on a local B200.")
-    ap.add_argument("--m", type=int, default=16384, help="Number of input rows (default: 16384)")
-    ap.add_argument("--k", type=int, default=16384, help="Number of input columns (default: 16384)")
+    ap.add_argument("--m", type=int, default=16384, help="rows of X")
+    ap.add_argument("--k", type=int, default=16384, help="columns of X (the scale blocks run along them)")
     ap.add_argument("--input-dtype", type=str, default="bf16", choices=["bf16", "fp16"])
     ap.add_argument("--warmup-iterations", type=int, default=10)
     ap.add_argument("--iterations", type=int, default=50)

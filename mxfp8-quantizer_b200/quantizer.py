@@ -370,37 +370,41 @@ def reference_quantize(x_padded: torch.Tensor):
 
 
 def decode_scale_bytes(s_bytes: torch.Tensor, m: int, k: int) -> torch.Tensor:
-    """Packed chunk layout -> dense (m, ceil(k/32)) scale bytes
-    (the layout map of MXFP8_quantizer.py:643-662)."""
-    scale_cols = ceil_div(k, SCALE_VEC_SIZE)
-    packed_col_blocks = ceil_div(scale_cols, SCALE_PACK_COLS)
-    rows = torch.arange(m, device=s_bytes.device)[:, None]
-    cols = torch.arange(scale_cols, device=s_bytes.device)[None, :]
-    rr = rows % SCALE_ROWS_PER_PACK
-    offs = ((rows // SCALE_ROWS_PER_PACK) * packed_col_blocks + cols // SCALE_PACK_COLS) * 512 \
-        + (rr % 32) * 16 + (rr // 32) * 4 + cols % SCALE_PACK_COLS
-    return s_bytes[offs]
+    """Packed chunk layout -> dense (m, ceil(k/32)) scale bytes (the layout
+    map of MXFP8_quantizer.py:643-662): block (r, c) sits in chunk
+    (r / 128, c / 4), 512 bytes each, row-block major, at byte
+    (r % 32) * 16 + (r % 128) / 32 * 4 + c % 4 of its chunk."""
+    n_blocks = ceil_div(k, SCALE_VEC_SIZE)
+    chunks_per_row_block = ceil_div(n_blocks, SCALE_PACK_COLS)
+    r = torch.arange(m, device=s_bytes.device).view(-1, 1)
+    c = torch.arange(n_blocks, device=s_bytes.device).view(1, -1)
+    chunk = (r // SCALE_ROWS_PER_PACK) * chunks_per_row_block + c // SCALE_PACK_COLS
+    within = (r % 32) * 16 + (r % SCALE_ROWS_PER_PACK) // 32 * 4 + c % SCALE_PACK_COLS
+    return s_bytes[chunk * (SCALE_ROWS_PER_PACK * SCALE_PACK_COLS) + within]
 
 
 def verify_quantizer_outputs(buffers, kernel_m: int, kernel_k: int, real_m: int, real_k: int):
-    """Compare Q/S with the torch restatement over the real region
-    (MXFP8_quantizer.py:664-697): S bit-exact, Q within Q_BYTE_DIFF_TOLERANCE."""
-    x = buffers["x"]
-    x_padded = torch.zeros((kernel_m, kernel_k), dtype=x.dtype, device=x.device)
-    x_padded[: x.shape[0], : x.shape[1]] = x
-    scale_ref, q_ref = reference_quantize(x_padded)
-    q_bytes = buffers["q_fp8"].view(torch.uint8).to(torch.int32)
-    q_diff = (q_bytes - q_ref.view(torch.uint8).to(torch.int32)).abs()[:real_m, :real_k]
-    q_max_byte_diff = int(q_diff.max().item())
-    q_exact_fraction = float((q_diff == 0).float().mean().item())
-    dense = decode_scale_bytes(buffers["s_storage_bytes"], kernel_m, kernel_k)
-    real_cols = ceil_div(real_k, SCALE_VEC_SIZE)
-    scale_bytes_exact = bool((dense[:real_m, :real_cols].to(torch.int32) == scale_ref[:real_m, :real_cols]).all().item())
+    """Check Q and S against the torch restatement on the real (m, k) region
+    (the rule of MXFP8_quantizer.py:664-697): every scale byte equal, every
+    payload byte within Q_BYTE_DIFF_TOLERANCE byte values."""
+    src = buffers["x"]
+    padded = src.new_zeros((kernel_m, kernel_k))
+    padded[: src.shape[0], : src.shape[1]] = src
+    want_scales, want_q = reference_quantize(padded)
+    # payload: byte distance on the real region
+    got = buffers["q_fp8"].view(torch.uint8)[:real_m, :real_k].to(torch.int16)
+    dist = (got - want_q.view(torch.uint8)[:real_m, :real_k].to(torch.int16)).abs()
+    worst = int(dist.max().item())
+    exact_share = (dist == 0).sum().item() / dist.numel()
+    # scales: the real blocks, read out of the packed storage
+    n_blocks = ceil_div(real_k, SCALE_VEC_SIZE)
+    stored = decode_scale_bytes(buffers["s_storage_bytes"], kernel_m, kernel_k)[:real_m, :n_blocks]
+    scales_ok = torch.equal(stored.to(torch.int32), want_scales[:real_m, :n_blocks].to(torch.int32))
     return {
-        "verification_passed": scale_bytes_exact and q_max_byte_diff <= Q_BYTE_DIFF_TOLERANCE,
-        "q_max_byte_diff": q_max_byte_diff,
-        "q_exact_fraction": q_exact_fraction,
-        "scale_bytes_exact": scale_bytes_exact,
+        "verification_passed": scales_ok and worst <= Q_BYTE_DIFF_TOLERANCE,
+        "q_max_byte_diff": worst,
+        "q_exact_fraction": float(exact_share),
+        "scale_bytes_exact": bool(scales_ok),
     }
 
 
@@ -409,23 +413,24 @@ def verify_quantizer_outputs(buffers, kernel_m: int, kernel_k: int, real_m: int,
 # --------------------------------------------------------------------------
 
 def prepare_and_quantize(m: int, k: int, dtype_name: str, seed: int, stream=None) -> dict[str, Any]:
-    """Quantize one seeded (m, k) matrix end to end: shape, launch, verify
-    (MXFP8_quantizer.py:809-861)."""
-    torch.manual_seed(seed)
-    torch_dtype = _resolve_input_dtype(dtype_name)
+    """One seeded (m, k) matrix through the quantizer and its check: the
+    reference's lower-level entry (MXFP8_quantizer.py:809-861).  X is drawn
+    with torch.randn on the GPU right after seeding, as the reference draws it,
+    so both see the same matrix."""
+    dtype = _resolve_input_dtype(dtype_name)
     kernel_m, kernel_k, _, _ = shape_problem(m, k, DEFAULT_ROWS_PER_CTA, DEFAULT_K_TILE)
-    x = torch.randn((m, k), dtype=torch_dtype, device="cuda")
-    buffers = materialize_quantizer_buffers(kernel_m, kernel_k, torch_dtype, x)
-    compiled = CompiledQuantizer(torch_dtype, m, k, buffers["x"].stride(0))
-    compiled(buffers["x_ptr"], buffers["q_dwords_ptr"], buffers["s_words_ptr"], kernel_m, kernel_k,
-             buffers["s_storage_word_count"], stream)
-    torch.cuda.synchronize()
-    check_cuda_launch_errors(stream, "quantizer launch")
-    verify = verify_quantizer_outputs(buffers, kernel_m, kernel_k, m, k)
-    if not verify["verification_passed"]:
-        raise ValueError(f"quantizer verification failed for ({m}, {k}): {verify}")
+    torch.manual_seed(seed)
+    x = torch.randn((m, k), dtype=dtype, device="cuda")
+    buffers = materialize_quantizer_buffers(kernel_m, kernel_k, dtype, x)
+    launch = CompiledQuantizer(dtype, m, k, buffers["x"].stride(0))
+    launch(buffers["x_ptr"], buffers["q_dwords_ptr"], buffers["s_words_ptr"], kernel_m, kernel_k,
+           buffers["s_storage_word_count"], stream)
+    check_cuda_launch_errors(stream, "quantizer launch")  # synchronises
+    stats = verify_quantizer_outputs(buffers, kernel_m, kernel_k, m, k)
+    if not stats["verification_passed"]:
+        raise ValueError(f"quantizer verification failed for ({m}, {k}): {stats}")
     return {"m": m, "k": k, "kernel_m": kernel_m, "kernel_k": kernel_k, "x": x, "buffers": buffers,
-            "compiled": compiled, "verify": verify}
+            "compiled": launch, "verify": stats}
 
 
 def _l2_bytes() -> int:
@@ -461,77 +466,76 @@ def benchmark_compiled_quantizer(launch, stream: torch.cuda.Stream, warmup: int,
             "min_runtime_s": mn * 1e-6, "mean_runtime_s": mean * 1e-6, "std_runtime_s": std * 1e-6}
 
 
+def _bytes_moved(rows: int, cols: int) -> int:
+    """2 bytes read, 1 payload byte and 1/32 scale byte written per element:
+    the reference's effective-bytes rule (MXFP8_quantizer.py:963-968)."""
+    return 3 * rows * cols + rows * (cols // SCALE_VEC_SIZE)
+
+
+def _check_once(compiled, args, buffers, kernel_m: int, kernel_k: int, m: int, k: int, stream: int) -> dict:
+    """One launch on the seeded X, checked before any timing, so a wrong
+    kernel never produces numbers (MXFP8_quantizer.py:912-941); the failure
+    message is the reference's."""
+    compiled(*args)
+    check_cuda_launch_errors(stream, "quantizer verification launch")
+    stats = verify_quantizer_outputs(buffers, kernel_m, kernel_k, m, k)
+    if not stats["verification_passed"]:
+        raise ValueError(
+            "MXFP8 quantizer correctness check FAILED: "
+            f"scale bytes bit-exact={stats['scale_bytes_exact']}, "
+            f"fp8 payload max byte diff={stats['q_max_byte_diff']} (tolerance {Q_BYTE_DIFF_TOLERANCE}), "
+            f"exact byte fraction={stats['q_exact_fraction']:.6f}")
+    print(f"quantizer output verified: scale bytes exact, payload bytes at most {stats['q_max_byte_diff']} apart "
+          f"({stats['q_exact_fraction']:.6f} identical)")
+    return stats
+
+
 def run_quantizer(m: int = 16384, k: int = 16384, rows_per_cta: int = DEFAULT_ROWS_PER_CTA,
                   k_tile: int = DEFAULT_K_TILE, input_dtype: str = "bf16", warmup_iterations: int = 10,
                   iterations: int = 50, benchmark_repeats: int = 5, cold_l2: bool = False,
                   skip_verification: bool = False, seed: int = 0) -> dict[str, Any]:
-    """Quantize + verify + benchmark one (m, k) problem (MXFP8_quantizer.py:863-1035)."""
+    """Quantize, check and time one seeded (m, k) problem: the reference's
+    benchmark entry (MXFP8_quantizer.py:863-1035), same arguments, result keys
+    and timing rule."""
     torch.manual_seed(seed)
-    dtype_name = input_dtype.lower()
-    torch_dtype = _resolve_input_dtype(input_dtype)
-    cfg = MXFP8QuantizerConfig(torch_dtype, rows_per_cta, k_tile)
+    dtype = _resolve_input_dtype(input_dtype)
+    cfg = MXFP8QuantizerConfig(dtype, rows_per_cta, k_tile)
     cfg.validate()
-    x = torch.randn((m, k), dtype=torch_dtype, device="cuda")
-    stream_obj = torch.cuda.current_stream()
-    stream = stream_obj.cuda_stream
-    is_full_tile = (m % rows_per_cta == 0) and (k % k_tile == 0)
+    x = torch.randn((m, k), dtype=dtype, device="cuda")
+    stream = torch.cuda.current_stream()
     kernel_m, kernel_k, grid_m, grid_k = shape_problem(m, k, rows_per_cta, k_tile)
-    buffers = materialize_quantizer_buffers(kernel_m, kernel_k, torch_dtype, x)
-    compiled = CompiledQuantizer(torch_dtype, m, k, buffers["x"].stride(0))
+    full_tile = m % rows_per_cta == 0 and k % k_tile == 0
+    compiled = CompiledQuantizer(dtype, m, k, x.stride(0))
 
-    def args_of(b):
-        return (b["x_ptr"], b["q_dwords_ptr"], b["s_words_ptr"], kernel_m, kernel_k, b["s_storage_word_count"],
-                stream)
+    def workspace(src: torch.Tensor):
+        b = materialize_quantizer_buffers(kernel_m, kernel_k, dtype, src)
+        return b, (b["x_ptr"], b["q_dwords_ptr"], b["s_words_ptr"], kernel_m, kernel_k, b["s_storage_word_count"],
+                   stream.cuda_stream)
 
-    verify_results = None
-    if not skip_verification:
-        compiled(*args_of(buffers))
-        torch.cuda.synchronize()
-        check_cuda_launch_errors(stream, "quantizer verification launch")
-        verify_results = verify_quantizer_outputs(buffers, kernel_m, kernel_k, m, k)
-        if not verify_results["verification_passed"]:
-            raise ValueError(
-                "MXFP8 quantizer correctness check FAILED: "
-                f"scale bytes bit-exact={verify_results['scale_bytes_exact']}, "
-                f"fp8 payload max byte diff={verify_results['q_max_byte_diff']} "
-                f"(tolerance {Q_BYTE_DIFF_TOLERANCE}), "
-                f"exact byte fraction={verify_results['q_exact_fraction']:.6f}")
-        print("Correctness check passed: "
-              f"scale bytes bit-exact={verify_results['scale_bytes_exact']}, "
-              f"fp8 payload max byte diff={verify_results['q_max_byte_diff']}, "
-              f"exact byte fraction={verify_results['q_exact_fraction']:.6f}")
-
-    logical_bytes_moved = 2 * m * k + m * k + m * (k // SCALE_VEC_SIZE)
-    physical_bytes_moved = 2 * kernel_m * kernel_k + kernel_m * kernel_k + kernel_m * (kernel_k // SCALE_VEC_SIZE)
-    one_workspace_bytes = (x.numel() * x.element_size() + buffers["q_bytes"].numel()
-                           + buffers["s_storage_bytes"].numel())
-    workspace_count = 1
-    if cold_l2:
-        workspace_count = min(warmup_iterations + iterations, (_l2_bytes() * 3) // one_workspace_bytes + 1)
-    workspaces = [args_of(buffers)]
-    keep = [buffers]
-    for _ in range(workspace_count - 1):
-        wx = torch.randn((m, k), dtype=torch_dtype, device="cuda")
-        wb = materialize_quantizer_buffers(kernel_m, kernel_k, torch_dtype, wx)
-        keep.append(wb)
-        workspaces.append(args_of(wb))
-    if workspace_count > 1:  # flush L2 after creating the workspaces
-        flush = torch.empty(_l2_bytes() * 2 // 4, dtype=torch.int32, device="cuda")
-        flush.zero_()
-        del flush
-    timing = benchmark_compiled_quantizer(compiled, stream_obj, warmup_iterations, iterations, workspaces,
+    first, first_args = workspace(x)
+    stats = None if skip_verification else _check_once(compiled, first_args, first, kernel_m, kernel_k, m, k,
+                                                       stream.cuda_stream)
+    # cold L2: distinct workspaces covering three times L2, then one L2 flush
+    ws_bytes = x.numel() * x.element_size() + first["q_bytes"].numel() + first["s_storage_bytes"].numel()
+    count = min(warmup_iterations + iterations, 3 * _l2_bytes() // ws_bytes + 1) if cold_l2 else 1
+    sets = [(first, first_args)] + [workspace(torch.randn((m, k), dtype=dtype, device="cuda"))
+                                    for _ in range(count - 1)]
+    if count > 1:
+        torch.empty(_l2_bytes() // 2, dtype=torch.int32, device="cuda").zero_()
+    timing = benchmark_compiled_quantizer(compiled, stream, warmup_iterations, iterations, [a for _, a in sets],
                                           benchmark_repeats)
-    check_cuda_launch_errors(stream, "quantizer benchmark")
-    rmin, rmean, rstd = timing["min_runtime_s"], timing["mean_runtime_s"], timing["std_runtime_s"]
-    v = verify_results
+    check_cuda_launch_errors(stream.cuda_stream, "quantizer benchmark")
+    logical, physical = _bytes_moved(m, k), _bytes_moved(kernel_m, kernel_k)
+    t_min, t_mean = timing["min_runtime_s"], timing["mean_runtime_s"]
+    checked = stats is not None
     return {
         "launch_success": True,
-        "verification_ran": v is not None,
-        "verification_passed": v["verification_passed"] if v is not None else None,
-        "q_max_byte_diff": v["q_max_byte_diff"] if v is not None else None,
-        "q_exact_fraction": v["q_exact_fraction"] if v is not None else None,
-        "scale_bytes_exact": v["scale_bytes_exact"] if v is not None else None,
-        "input_dtype": dtype_name,
+        "verification_ran": checked,
+        "verification_passed": stats["verification_passed"] if checked else None,
+        "q_max_byte_diff": stats["q_max_byte_diff"] if checked else None,
+        "q_exact_fraction": stats["q_exact_fraction"] if checked else None,
+        "scale_bytes_exact": stats["scale_bytes_exact"] if checked else None,
+        "input_dtype": input_dtype.lower(),
         "rows_per_cta": cfg.rows_per_cta,
         "k_tile": cfg.k_tile,
         "threads_per_cta": cfg.threads_per_cta,
@@ -541,22 +545,22 @@ def run_quantizer(m: int = 16384, k: int = 16384, rows_per_cta: int = DEFAULT_RO
         "grid_m": grid_m,
         "grid_k": grid_k,
         "total_ctas": grid_m * grid_k,
-        "runtime_min_s": rmin,
-        "runtime_mean_s": rmean,
-        "runtime_std_s": rstd,
+        "runtime_min_s": t_min,
+        "runtime_mean_s": t_mean,
+        "runtime_std_s": timing["std_runtime_s"],
         "runtime_min_us": timing["min_runtime_us"],
         "runtime_mean_us": timing["mean_runtime_us"],
         "runtime_std_us": timing["std_runtime_us"],
-        "effective_gb_s": logical_bytes_moved / rmin / 1.0e9,
-        "effective_gb_s_mean": logical_bytes_moved / rmean / 1.0e9,
-        "effective_tb_s": logical_bytes_moved / rmin / 1.0e12,
-        "logical_bytes_moved": logical_bytes_moved,
-        "physical_bytes_moved": physical_bytes_moved,
+        "effective_gb_s": logical / t_min / 1.0e9,
+        "effective_gb_s_mean": logical / t_mean / 1.0e9,
+        "effective_tb_s": logical / t_min / 1.0e12,
+        "logical_bytes_moved": logical,
+        "physical_bytes_moved": physical,
         "benchmark_repeats": benchmark_repeats,
-        "workspace_count": workspace_count,
+        "workspace_count": count,
         "cold_l2": cold_l2,
-        "is_full_tile": is_full_tile,
-        "dispatch_mode": "b200_tma_full_tile" if is_full_tile else "b200_tma_ragged",
+        "is_full_tile": full_tile,
+        "dispatch_mode": "b200_tma_full_tile" if full_tile else "b200_tma_ragged",
     }
 
 
@@ -567,48 +571,60 @@ def blockscaled_gemm(a_q: torch.Tensor, b_q: torch.Tensor, a_s: torch.Tensor, b_
                             scale_b=b_s.view(torch.float8_e8m0fnu), out_dtype=torch.float32)
 
 
+def _check_gemm_config(m: int, n: int, k: int, tiler: tuple[int, int], cluster: tuple[int, int]) -> None:
+    """The block-scaled GEMM consumer's shape rules, with the reference's
+    messages (MXFP8_quantizer.py:1058-1095)."""
+    tm, tn = tiler
+    cm, cn = cluster
+    if tm not in (128, 256) or tn not in (64, 128, 192, 256):
+        raise ValueError(f"mma_tiler_mn must be M in (128, 256) and N in (64, 128, 192, 256), got {tiler}")
+    if any(v <= 0 or v & (v - 1) or v > 4 for v in (cm, cn)) or cm * cn > 16:
+        raise ValueError(f"cluster_shape_mn entries must be powers of two in [1, 4] with a product <= 16, "
+                         f"got {cluster}")
+    if tm == 256 and cm % 2:
+        raise ValueError(f"cluster_shape_mn[0] must be a multiple of 2 when mma_tiler_mn[0] == 256, "
+                         f"got cluster_shape_mn={cluster}")
+    if m % tm or n % tn:
+        raise ValueError(f"GEMM consumer requires M % {tm} == 0 and N % {tn} == 0 for mma_tiler_mn={tiler}, "
+                         f"got m={m}, n={n}")
+    if k % DEFAULT_K_TILE:
+        raise ValueError(f"GEMM consumer requires K % {DEFAULT_K_TILE} == 0, got k={k}")
+
+
+def _dequantized(q: torch.Tensor, s_bytes: torch.Tensor, rows: int, k: int) -> torch.Tensor:
+    """fp32 (rows, k) = e4m3 payload times 2^(scale byte - 127), decoded on the host side."""
+    scale = torch.exp2(decode_scale_bytes(s_bytes, rows, k).to(torch.float32) - 127.0)
+    return q.to(torch.float32) * scale.repeat_interleave(SCALE_VEC_SIZE, dim=1)[:, :k]
+
+
+def _error_stats(c: torch.Tensor, ref: torch.Tensor, tol: float) -> tuple[float, float, float]:
+    """(max |c - ref|, max |c - ref| / (tol + tol |ref|), 1 / that ratio): the
+    end-to-end metrics the reference reports (MXFP8_quantizer.py:1189-1194)."""
+    err = (c - ref).abs()
+    ratio = float((err / (tol * (1.0 + ref.abs()))).max().item())
+    return float(err.max().item()), ratio, (1.0 / ratio if ratio > 0 else float("inf"))
+
+
 def run_e2e_verification(m: int = 1024, n: int = 1024, k: int = 2048, input_dtype: str = "bf16", seed: int = 0,
                          gemm_tolerance: float = 1.0e-2, mma_tiler_mn: tuple[int, int] = (128, 128),
                          cluster_shape_mn: tuple[int, int] = (1, 1)) -> dict[str, Any]:
-    """Quantize A (m, k) and B (n, k) and feed Q/S unmodified into a
-    block-scaled GEMM; compare with fp32 (MXFP8_quantizer.py:1037-1223)."""
-    if mma_tiler_mn[0] not in (128, 256) or mma_tiler_mn[1] not in (64, 128, 192, 256):
-        raise ValueError(f"mma_tiler_mn must be M in (128, 256) and N in (64, 128, 192, 256), got {mma_tiler_mn}")
-
-    def pow2(v):
-        return v > 0 and (v & (v - 1)) == 0
-
-    if (not pow2(cluster_shape_mn[0]) or not pow2(cluster_shape_mn[1]) or cluster_shape_mn[0] > 4
-            or cluster_shape_mn[1] > 4 or cluster_shape_mn[0] * cluster_shape_mn[1] > 16):
-        raise ValueError(f"cluster_shape_mn entries must be powers of two in [1, 4] with a product <= 16, "
-                         f"got {cluster_shape_mn}")
-    if mma_tiler_mn[0] == 256 and cluster_shape_mn[0] % 2 != 0:
-        raise ValueError(f"cluster_shape_mn[0] must be a multiple of 2 when mma_tiler_mn[0] == 256, "
-                         f"got cluster_shape_mn={cluster_shape_mn}")
-    if m % mma_tiler_mn[0] != 0 or n % mma_tiler_mn[1] != 0:
-        raise ValueError(f"GEMM consumer requires M % {mma_tiler_mn[0]} == 0 and N % {mma_tiler_mn[1]} == 0 "
-                         f"for mma_tiler_mn={mma_tiler_mn}, got m={m}, n={n}")
-    if k % DEFAULT_K_TILE != 0:
-        raise ValueError(f"GEMM consumer requires K % {DEFAULT_K_TILE} == 0, got k={k}")
+    """Quantize A (m, k) and B (n, k), feed Q and S unmodified into a
+    block-scaled GEMM and compare it with an fp32 GEMM of the decoded operands
+    (the check of MXFP8_quantizer.py:1037-1223; the consumer here is cuBLASLt
+    through torch._scaled_mm)."""
+    _check_gemm_config(m, n, k, mma_tiler_mn, cluster_shape_mn)
     torch.manual_seed(seed)
     stream = torch.cuda.current_stream().cuda_stream
-    a_res = prepare_and_quantize(m, k, input_dtype, seed, stream)
-    b_res = prepare_and_quantize(n, k, input_dtype, seed + 1, stream)
-    a_q, b_q = a_res["buffers"]["q_fp8"], b_res["buffers"]["q_fp8"]
-    a_s, b_s = a_res["buffers"]["s_storage_bytes"], b_res["buffers"]["s_storage_bytes"]
-    c = blockscaled_gemm(a_q, b_q, a_s, b_s)
+    a, b = (prepare_and_quantize(rows, k, input_dtype, sd, stream) for rows, sd in ((m, seed), (n, seed + 1)))
+    qa, sa = a["buffers"]["q_fp8"], a["buffers"]["s_storage_bytes"]
+    qb, sb = b["buffers"]["q_fp8"], b["buffers"]["s_storage_bytes"]
+    c = blockscaled_gemm(qa, qb, sa, sb)
     torch.cuda.synchronize()
-    sfa = torch.exp2(decode_scale_bytes(a_s, m, k).to(torch.float32) - 127.0).repeat_interleave(SCALE_VEC_SIZE, 1)[:, :k]
-    sfb = torch.exp2(decode_scale_bytes(b_s, n, k).to(torch.float32) - 127.0).repeat_interleave(SCALE_VEC_SIZE, 1)[:, :k]
-    ref = (a_q.to(torch.float32) * sfa) @ (b_q.to(torch.float32) * sfb).T
-    abs_err = (c - ref).abs()
-    max_abs_err = float(abs_err.max().item())
-    max_err_ratio = float((abs_err / (gemm_tolerance + gemm_tolerance * ref.abs())).max().item())
-    pass_margin = 1.0 / max_err_ratio if max_err_ratio > 0 else float("inf")
+    ref = _dequantized(qa, sa, m, k) @ _dequantized(qb, sb, n, k).T
+    max_abs_err, max_err_ratio, pass_margin = _error_stats(c, ref, gemm_tolerance)
     torch.testing.assert_close(c, ref, rtol=gemm_tolerance, atol=gemm_tolerance)
-    print("End-to-end blockscaled GEMM check passed: "
-          f"max_abs_err={max_abs_err:.3e}, max_err_ratio={max_err_ratio:.3f} "
-          f"(atol=rtol={gemm_tolerance:.0e}, pass margin={pass_margin:.1f}x)")
+    print(f"block-scaled GEMM on the quantizer's outputs matches fp32: {m}x{n}x{k} {input_dtype}, "
+          f"largest error {max_abs_err:.3e} = {max_err_ratio:.3f} of the tolerance ({pass_margin:.1f}x margin)")
     return {
         "e2e_verification_passed": True,
         "m": m, "n": n, "k": k, "input_dtype": input_dtype,
@@ -616,8 +632,8 @@ def run_e2e_verification(m: int = 1024, n: int = 1024, k: int = 2048, input_dtyp
                         "sf_vec_size": SCALE_VEC_SIZE, "sf_dtype": "Float8E8M0FNU", "a/b_dtype": "Float8E4M3FN",
                         "c_dtype": "Float32", "consumer": "torch._scaled_mm (cuBLASLt block-scaled, 128x4 chunks)"},
         "sfa_layout": "tcgen05_atom_layout_packed_direct",
-        "quantizer_verify_a": a_res["verify"],
-        "quantizer_verify_b": b_res["verify"],
+        "quantizer_verify_a": a["verify"],
+        "quantizer_verify_b": b["verify"],
         "max_abs_err": max_abs_err,
         "max_err_ratio": max_err_ratio,
         "pass_margin": pass_margin,
@@ -626,24 +642,23 @@ def run_e2e_verification(m: int = 1024, n: int = 1024, k: int = 2048, input_dtyp
 
 
 def run_e2e_suite(configs=DEFAULT_E2E_SUITE, gemm_tolerance: float = 1.0e-2) -> dict[str, Any]:
-    """Every config must pass (MXFP8_quantizer.py:1225-1289)."""
-    results = [run_e2e_verification(m=m, n=n, k=k, input_dtype=dt, seed=seed, gemm_tolerance=gemm_tolerance,
-                                    mma_tiler_mn=tiler, cluster_shape_mn=cluster)
-               for (m, n, k, dt, seed, tiler, cluster) in configs]
-    summary = []
-    for (m, n, k, dt, seed, tiler, cluster), r in zip(configs, results):
-        summary.append({"m": m, "n": n, "k": k, "input_dtype": dt, "seed": seed, "mma_tiler_mn": list(tiler),
-                        "cluster_shape_mn": list(cluster),
-                        "quantizer_verify_passed": r["quantizer_verify_a"]["verification_passed"]
-                        and r["quantizer_verify_b"]["verification_passed"],
-                        "max_abs_err": r["max_abs_err"], "max_err_ratio": r["max_err_ratio"],
-                        "pass_margin": r["pass_margin"]})
-    worst_abs = max(r["max_abs_err"] for r in results)
-    worst_ratio = max(r["max_err_ratio"] for r in results)
-    print(f"e2e suite passed: {len(results)}/{len(results)} configs "
-          f"(worst max_abs_err={worst_abs:.3e}, worst max_err_ratio={worst_ratio:.3f})")
-    return {"e2e_suite_passed": True, "num_configs": len(results), "gemm_tolerance": gemm_tolerance,
-            "configs": summary}
+    """run_e2e_verification over (m, n, k, dtype, seed, mma_tiler_mn,
+    cluster_shape_mn) configs; any failure raises (MXFP8_quantizer.py:1225-1289)."""
+    entries = []
+    for m, n, k, dt, seed, tiler, cluster in configs:
+        r = run_e2e_verification(m=m, n=n, k=k, input_dtype=dt, seed=seed, gemm_tolerance=gemm_tolerance,
+                                 mma_tiler_mn=tiler, cluster_shape_mn=cluster)
+        entry = dict(m=m, n=n, k=k, input_dtype=dt, seed=seed, mma_tiler_mn=list(tiler),
+                     cluster_shape_mn=list(cluster))
+        entry["quantizer_verify_passed"] = all(r[key]["verification_passed"]
+                                               for key in ("quantizer_verify_a", "quantizer_verify_b"))
+        entry.update({key: r[key] for key in ("max_abs_err", "max_err_ratio", "pass_margin")})
+        entries.append(entry)
+    worst = max(entries, key=lambda e: e["max_err_ratio"])
+    print(f"all {len(entries)} end-to-end configurations passed; closest to the tolerance: "
+          f"{worst['m']}x{worst['n']}x{worst['k']} {worst['input_dtype']} at {worst['max_err_ratio']:.3f}")
+    return {"e2e_suite_passed": True, "num_configs": len(entries), "gemm_tolerance": gemm_tolerance,
+            "configs": entries}
 
 
 def build_runtime() -> dict[str, Any]:
