@@ -104,25 +104,22 @@ def packed_scale_word_count(m: int, k: int, scale_vec_size: int = SCALE_VEC_SIZE
 
 
 def shape_problem(m: int, k: int, rows_per_cta: int = DEFAULT_ROWS_PER_CTA, k_tile: int = DEFAULT_K_TILE):
-    """Logical (m, k) -> the reference's padded launch shape, same limits and
-    messages as MXFP8_quantizer.py:766-791."""
-    if m < 1 or k < 1:
+    """Logical (m, k) -> (kernel_m, kernel_k, grid_m, grid_k), the reference's
+    padded launch shape, with its limits and messages (MXFP8_quantizer.py:766-791)."""
+    if min(m, k) < 1:
         raise ValueError(f"m and k must be >= 1, got m={m}, k={k}")
-    if m > _INT32_MAX or k > _INT32_MAX:
+    if max(m, k) > _INT32_MAX:
         raise ValueError(
             f"m and k must fit Int32 (<= {_INT32_MAX}) because they are passed "
             f"to the kernel as Int32 scalars, got m={m}, k={k}")
-    kernel_m = ceil_div(m, rows_per_cta) * rows_per_cta
-    kernel_k = ceil_div(k, k_tile) * k_tile
-    grid_m = kernel_m // rows_per_cta
-    grid_k = kernel_k // k_tile
+    grid_m, grid_k = ceil_div(m, rows_per_cta), ceil_div(k, k_tile)
     if grid_m > _INT32_MAX:
         raise ValueError(f"gridDim.x limit exceeded: {grid_m} row-tiles > {_INT32_MAX}")
     if grid_k > _GRID_DIM_Y_LIMIT:
         raise ValueError(
             f"gridDim.y limit exceeded: k={k} with k_tile={k_tile} needs "
             f"grid_k={grid_k} > {_GRID_DIM_Y_LIMIT} K-tiles. Reduce k_tile or reshape the problem.")
-    return kernel_m, kernel_k, grid_m, grid_k
+    return grid_m * rows_per_cta, grid_k * k_tile, grid_m, grid_k
 
 
 def _resolve_input_dtype(dtype_name: str) -> torch.dtype:
