@@ -408,6 +408,23 @@ def test_quantize_inside_cuda_graph(layout, capi, oracle_mod):
     del g
 
 
+# The reference README's published end-to-end results (README.md:162-169 of the reference): max abs error and
+# pass margin of its block-scaled GEMM on its quantizer's outputs, per DEFAULT_E2E_SUITE entry.
+PUBLISHED_E2E = [(1.07e-4, 650), (1.07e-4, 420), (3.36e-4, 265), (2.44e-4, 259), (1.07e-4, 440), (9.16e-5, 379)]
+
+
+def test_e2e_suite_reproduces_the_published_errors(capi):
+    """Same seeds, same inputs, bit-identical Q and S: the block-scaled GEMM
+    on this library's outputs lands on the reference's published errors and
+    margins (5 % allowed for the GEMM libraries' accumulation order)."""
+    import MXFP8_quantizer
+
+    r = MXFP8_quantizer.run_e2e_suite()
+    for got, (err, margin) in zip(r["configs"], PUBLISHED_E2E):
+        assert got["max_abs_err"] == pytest.approx(err, rel=0.05), got
+        assert got["pass_margin"] == pytest.approx(margin, rel=0.05), got
+
+
 def test_e2e_suite_all_configs(capi):
     import MXFP8_quantizer
 
