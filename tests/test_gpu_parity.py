@@ -599,3 +599,25 @@ def test_randomized_shapes_layouts_and_values(capi, oracle_mod):
             check_against_oracle(capi, oracle_mod, bits, dtype, **kw)
         else:
             check_against_oracle(capi, oracle_mod, bits, dtype, m, (k + 31) // 32 * 32, **kw)
+
+
+def test_reference_compatible_clis_run(capi):
+    """benchmark.py and e2e.py, run as the reference's users run its tools,
+    print their JSON summaries with a passing check."""
+    import json
+    import pathlib
+    import subprocess
+    import sys
+
+    root = pathlib.Path(__file__).resolve().parent.parent
+
+    def run(*argv):
+        out = subprocess.run([sys.executable, *argv], cwd=root, capture_output=True, text=True, timeout=600)
+        assert out.returncode == 0, out.stderr[-2000:]
+        return json.loads(out.stdout[out.stdout.index("{"):])
+
+    bench = run("benchmark.py", "--m", "1000", "--k", "4064", "--iterations", "5", "--benchmark-repeats", "2",
+                "--warmup-iterations", "2")
+    assert bench["verification_passed"] and bench["q_max_byte_diff"] == 0 and bench["effective_tb_s"] > 0
+    e2e = run("e2e.py", "--m", "256", "--n", "256", "--k", "512", "--input-dtype", "fp16")
+    assert e2e["e2e_verification_passed"] and e2e["max_err_ratio"] < 1.0
