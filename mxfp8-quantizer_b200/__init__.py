@@ -22,6 +22,7 @@ from .quantizer import (
     decode_scale_bytes,
     dequantize,
     materialize_quantizer_buffers,
+    pack_scale_bytes,
     packed_scale_storage_bytes,
     packed_scale_word_count,
     prepare_and_quantize,

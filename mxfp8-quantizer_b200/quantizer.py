@@ -380,6 +380,21 @@ def decode_scale_bytes(s_bytes: torch.Tensor, m: int, k: int) -> torch.Tensor:
     return s_bytes[chunk * (SCALE_ROWS_PER_PACK * SCALE_PACK_COLS) + within]
 
 
+def pack_scale_bytes(dense: torch.Tensor, m: int, k: int) -> torch.Tensor:
+    """Dense (m, ceil(k/32)) scale bytes -> packed storage of (m, k): the
+    inverse of decode_scale_bytes.  Bytes of the padding (rows up to the next
+    multiple of 128, scale columns up to the next multiple of 4) are 0."""
+    n_blocks = ceil_div(k, SCALE_VEC_SIZE)
+    chunks_per_row_block = ceil_div(n_blocks, SCALE_PACK_COLS)
+    r = torch.arange(m, device=dense.device).view(-1, 1)
+    c = torch.arange(n_blocks, device=dense.device).view(1, -1)
+    chunk = (r // SCALE_ROWS_PER_PACK) * chunks_per_row_block + c // SCALE_PACK_COLS
+    within = (r % 32) * 16 + (r % SCALE_ROWS_PER_PACK) // 32 * 4 + c % SCALE_PACK_COLS
+    out = torch.zeros(packed_scale_storage_bytes(m, k), dtype=torch.uint8, device=dense.device)
+    out[chunk * (SCALE_ROWS_PER_PACK * SCALE_PACK_COLS) + within] = dense.to(torch.uint8)
+    return out
+
+
 def verify_quantizer_outputs(buffers, kernel_m: int, kernel_k: int, real_m: int, real_k: int):
     """Check Q and S against the torch restatement on the real (m, k) region
     (the rule of MXFP8_quantizer.py:664-697): every scale byte equal, every

@@ -45,3 +45,18 @@ def max_over_ranks(value: float, device=None) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_over_ranks(value: float, device=None) -> list[float]:
+    """Every rank's value of a per-rank float, in rank order (a one-element
+    list when torch.distributed is not initialised).  Every rank must call
+    it, in the same order as its other collectives."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return [value]
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    parts = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, t)
+    return [float(p.item()) for p in parts]
