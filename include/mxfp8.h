@@ -75,9 +75,9 @@ MXFP8_API int mxfp8_launch_shape(int64_t m, int64_t k, int64_t* kernel_m, int64_
  * at any offset (16-byte stores when q, ld_q and s allow them, narrower or
  * realigned stores otherwise).  Empty x (m or k == 0) takes a plain-load
  * kernel that writes the padding.
- * The first call on a device allocates that device's 256-byte status word
- * (see mxfp8_device_status), so make it before any stream capture; later
- * calls allocate nothing.
+ * The first call on a device (and the first in each new CUDA context of it)
+ * allocates that device's 256-byte status word (see mxfp8_device_status), so
+ * make it before any stream capture; later calls allocate nothing.
  * Replaces the host pad copy + launch of materialize_quantizer_buffers and
  * the compiled kernel call, MXFP8_quantizer.py:554-608 and 914-922. */
 MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int64_t k, int64_t ld_x,
@@ -89,20 +89,22 @@ MXFP8_API int mxfp8_quantize(const void* x, int dtype, int64_t m, int64_t k, int
  * No counterpart in the reference.
  * Who needs it: callers that may not call cudaMalloc.  mxfp8_quantize
  * allocates a 256-byte status buffer on its first call on each device, which
- * fails or is forbidden for code that runs while a CUDA graph is being
- * captured, for plugins whose host owns all device memory through its own
- * pool or arena, and on a device whose memory another allocator has already
- * reserved in full.
- * How: the quantize kernel's only scratch, one 32-bit status word written
- * when a pipeline wait times out, lives in a fixed 256-byte device array of
- * the library (64 words; every GPU that loads the library holds it until
- * exit).  A call needs 1 word, so no problem size exceeds the array.  The
- * first call on each device looks up the array's device address (no
- * allocation); make that first call before any stream capture.  Each call
- * clears the word in stream order before its kernel runs.  All calls share
- * the array, so calls whose kernels overlap on the GPU (different streams)
- * race on that word; its contents are not readable through this API
- * (mxfp8_device_status reports only the mxfp8_quantize word). */
+ * fails or is forbidden for plugins whose host owns all device memory
+ * through its own pool or arena, for code whose allocations must all be made
+ * up front (real-time or certified pipelines), and on a device whose memory
+ * another allocator has already reserved in full.
+ * How: the quantize kernel's only scratch, one 32-bit status word that a
+ * pipeline wait which times out marks, lives in a fixed 256-byte device
+ * array of the library (64 words; every GPU that loads the library holds it
+ * until exit).  A call needs 1 word, so no problem size exceeds the array.
+ * The first call on each device (and the first after its CUDA context
+ * changed) looks up the array's device address with cudaGetSymbolAddress,
+ * which allocates nothing; make that first call before any stream capture.
+ * The word is sticky: calls only set bits in it, and
+ * mxfp8_noalloc_status reads it (and clears it on request).  All calls on a
+ * device share the word, so after calls whose kernels overlap on the GPU
+ * (different streams) a set bit cannot be attributed to one of them, and a
+ * clear that runs while such a kernel is in flight can lose its report. */
 MXFP8_API int mxfp8_quantize_noalloc(const void* x, int dtype, int64_t m, int64_t k, int64_t ld_x,
                                      void* q, int64_t q_rows, int64_t q_cols, int64_t ld_q,
                                      void* s, int64_t s_bytes, mxfp8_stream_t stream);
@@ -132,11 +134,20 @@ MXFP8_API int mxfp8_dequantize(const void* q, int64_t rows, int64_t cols, int64_
  * bit here and the kernel returns early.  Bits: 1 = payload tile wait,
  * 2 = stage-release wait, 4 = drain wait on exit, 8 = the self-test's wait,
  * 16 = a store outside its output was skipped (only the checked build,
- * include/mxfp8_checked.h, tests stores).  Reading synchronises the
- * device; clear != 0 resets the word.  The word lives in a small device
- * buffer allocated on the first quantize call on each device.
+ * include/mxfp8_checked.h, tests stores).  Reading waits for the device
+ * (cudaDeviceSynchronize); clear != 0 resets the word.  The word lives in a
+ * small device buffer allocated on the first call on each device (and in
+ * each new CUDA context of it).  Calls of mxfp8_quantize_noalloc report to
+ * their own word instead (mxfp8_noalloc_status).
  * No counterpart in the reference (its kernel waits without a limit). */
 MXFP8_API int mxfp8_device_status(uint32_t* status_out, int clear);
+
+/* The status word of mxfp8_quantize_noalloc calls on the current device:
+ * same bits and same reading rules as mxfp8_device_status (waits for the
+ * device; clear != 0 resets the word), read from the library's fixed device
+ * array, so this allocates no device memory either.
+ * No counterpart in the reference (its kernel waits without a limit). */
+MXFP8_API int mxfp8_noalloc_status(uint32_t* status_out, int clear);
 
 /* Failure-path self-test: launches one CTA that waits, with the same bounded
  * wait the quantizer pipeline uses, on an mbarrier nothing completes; after

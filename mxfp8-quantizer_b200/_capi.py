@@ -38,6 +38,7 @@ EXPORTS = (
     "mxfp8_quantize_padded",
     "mxfp8_dequantize",
     "mxfp8_device_status",
+    "mxfp8_noalloc_status",
     "mxfp8_selftest_bounded_wait",
     "mxfp8_strerror",
     "mxfp8_last_error",
@@ -68,6 +69,8 @@ def configure(L: ctypes.CDLL) -> ctypes.CDLL:
     L.mxfp8_dequantize.restype = i32
     L.mxfp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]
     L.mxfp8_device_status.restype = i32
+    L.mxfp8_noalloc_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), i32]
+    L.mxfp8_noalloc_status.restype = i32
     L.mxfp8_selftest_bounded_wait.argtypes = [ctypes.c_uint32, vp]
     L.mxfp8_selftest_bounded_wait.restype = i32
     L.mxfp8_strerror.argtypes = [i32]
@@ -165,6 +168,13 @@ def dequantize(q_ptr: int, rows: int, cols: int, ld_q: int, s_ptr: int, s_bytes:
 def device_status(clear: bool = False) -> int:
     v = ctypes.c_uint32(0)
     check(lib().mxfp8_device_status(ctypes.byref(v), int(clear)), "device status read")
+    return int(v.value)
+
+
+def noalloc_status(clear: bool = False) -> int:
+    """Status word of the allocation-free entry on the current device."""
+    v = ctypes.c_uint32(0)
+    check(lib().mxfp8_noalloc_status(ctypes.byref(v), int(clear)), "allocation-free status read")
     return int(v.value)
 
 

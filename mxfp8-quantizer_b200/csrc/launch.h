@@ -37,4 +37,15 @@ int launch_bounded_wait_selftest(unsigned int* status, uint32_t limit_us, cudaSt
 // Records the CUDA error text for mxfp8_last_error() on this host thread.
 void set_last_error(const char* what, int code);
 
+// Key of the CUDA context current on this host thread, unique for the
+// process's lifetime; 0 if none is current (context_key) or after binding the
+// runtime's context to the thread first (bound_context_key, never 0 on
+// success).  Per-device caches compare it to notice a new context.
+int context_key(uint64_t* key);
+int bound_context_key(uint64_t* key);
+
+// Device address of the allocation-free entries' status word (a fixed device
+// array of quantize_tma.cu) on device `dev`, the current device.
+int noalloc_status_word(int dev, unsigned int** out);
+
 }  // namespace mxfp8

@@ -255,13 +255,16 @@ __global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
                 const int chunk = lane & 7;
                 const int grow = rt * kTileRows + row;
                 // loaded before any branch, so the loads of all 4 iterations can be in flight together
-                const uint4 v = *reinterpret_cast<const uint4*>(qbuf + row * 128 + ((chunk ^ stage_key<ROWS>(row)) << 4));
+                const uint8_t* srow = qbuf + row * 128;
+                const uint32_t key = stage_key<ROWS>(row);
+                const uint4 v = *reinterpret_cast<const uint4*>(srow + ((chunk ^ key) << 4));
                 if constexpr (QU) {
-                    if (grow < p.q_rows) {
-                        const int seg = p.q_cols - ct * kTileCols < kTileCols ? p.q_cols - ct * kTileCols : kTileCols;
-                        store_row_any(p.q + (int64_t)grow * p.ld_q + ct * kTileCols, v, qbuf + row * 128,
-                                      stage_key<ROWS>(row), seg, chunk, p.qw, p.status);
-                    }
+                    uint8_t* dst = p.q + (int64_t)grow * p.ld_q + ct * kTileCols;
+                    const int seg = p.q_cols - ct * kTileCols < kTileCols ? p.q_cols - ct * kTileCols : kTileCols;
+                    uint4 vn = v;
+                    if (reinterpret_cast<uintptr_t>(dst) & 3)  // realigned row: the next chunk too
+                        vn = *reinterpret_cast<const uint4*>(srow + ((next_chunk(chunk) ^ key) << 4));
+                    if (grow < p.q_rows) store_row_any(dst, v, vn, srow, key, seg, chunk, p.qw, p.status);
                 } else {
                     const int col = ct * kTileCols + chunk * 16;  // q_cols % 32 == 0: a chunk is all in or all out
                     if (grow < p.q_rows && col < p.q_cols)
@@ -387,6 +390,7 @@ static int encode_x_maps(const QuantizeArgs& a, XMaps<ROWS>& xm) {
 template <int DT, bool ROWS, bool QU>
 static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
     constexpr int kSt = ROWS ? kRowStages : kStages;
+    constexpr int kCtasPerSm = ROWS ? kRowCtasPerSm : 1;
     using L = Layout<kSt, ROWS>;
     auto kernel = quantize_tma_kernel<DT, kSt, ROWS, QU>;
     // The shared-memory opt-in is per device: set it once per device, so that
@@ -443,7 +447,7 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
         const int64_t nr = n_row_tiles - r0 < rows_per_launch ? n_row_tiles - r0 : rows_per_launch;
         p.rt_offset = (int)r0;
         p.n_tiles = (int)(nr * a.col_chunks);
-        const int ctas = sm_count * (ROWS ? kRowCtasPerSm : 1);
+        const int ctas = sm_count * kCtasPerSm;
         const int grid = p.n_tiles < ctas ? p.n_tiles : ctas;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
@@ -486,11 +490,14 @@ int launch_quantize_tma(const QuantizeArgs& a, int sm_count, cudaStream_t stream
 }
 
 // ---------------------------------------------------------------------------
-// Allocation-free launch.  The kernel above needs one word of global scratch
-// (its status word for bounded-wait timeouts).  mxfp8_quantize keeps that
-// word in a buffer it allocates on the first call on each device; this
-// variant keeps it in a fixed device array of this file instead, so it never
+// Allocation-free launch.  The kernel above needs one word of global scratch:
+// its status word, which a bounded wait that times out (or, in the checked
+// build, a skipped store) marks with atomicOr.  mxfp8_quantize keeps that word
+// in a buffer it allocates on its first call on each device; this variant
+// keeps it in a fixed device array of this file instead, so it never
 // allocates.  Every GPU that loads the library holds the array until exit.
+// The word is sticky: calls only set bits; mxfp8_noalloc_status reads it and
+// clears it on request.  A static __device__ array starts at zero.
 // ---------------------------------------------------------------------------
 
 constexpr int kNoAllocScratchWords = 64;  // 256 bytes per device
@@ -498,43 +505,47 @@ constexpr int kStatusWordsPerCall = 1;
 constexpr int kMaxNoAllocDevices = 64;
 static __device__ __align__(256) unsigned int g_noalloc_scratch[kNoAllocScratchWords];
 
+struct NoAllocSlot {
+    uint64_t ctx;        // context_key() the address was looked up in
+    unsigned int* addr;  // device address of g_noalloc_scratch there
+};
 static std::mutex g_noalloc_mu;
-static unsigned int* g_noalloc_addr[kMaxNoAllocDevices];
+static NoAllocSlot g_noalloc_slot[kMaxNoAllocDevices];
 
 // Device address of g_noalloc_scratch on device `dev` (the current device),
-// looked up once per device.  In host code the array's name is only a
-// host-side stand-in; the kernel must be given this address.
-static int noalloc_scratch(int dev, unsigned int** out) {
+// looked up once per device and context: the first call on a device, and the
+// first after its context changed (cudaDeviceReset, another driver-API
+// context made current), calls cudaGetSymbolAddress, which allocates nothing.
+// In host code the array's name is only a host-side stand-in; kernels must be
+// given this address.
+int noalloc_status_word(int dev, unsigned int** out) {
+    static_assert(kStatusWordsPerCall <= kNoAllocScratchWords, "scratch array too small");
     if (dev < 0 || dev >= kMaxNoAllocDevices) {
         set_last_error("device index beyond the allocation-free table", 0);
         return MXFP8_ERR_DEVICE;
     }
+    uint64_t ctx = 0;
+    if (int rc = bound_context_key(&ctx)) return rc;
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
+    NoAllocSlot& slot = g_noalloc_slot[dev];
+    if (!slot.addr || slot.ctx != ctx) {
         void* ptr = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
         if (e != cudaSuccess || !ptr) {
             set_last_error("cudaGetSymbolAddress(g_noalloc_scratch)", (int)e);
             return MXFP8_ERR_CUDA;
         }
-        g_noalloc_addr[dev] = static_cast<unsigned int*>(ptr);
+        slot.addr = static_cast<unsigned int*>(ptr);
+        slot.ctx = ctx;
     }
-    *out = g_noalloc_addr[dev];
+    *out = slot.addr;
     return MXFP8_OK;
 }
 
 int launch_quantize_tma_noalloc(const QuantizeArgs& args, int dev, int sm_count, cudaStream_t stream) {
-    static_assert(kStatusWordsPerCall <= kNoAllocScratchWords, "scratch array too small");
     unsigned int* scratch = nullptr;
-    int rc = noalloc_scratch(dev, &scratch);
+    int rc = noalloc_status_word(dev, &scratch);
     if (rc) return rc;
-    // The array keeps the previous call's contents: the status word must
-    // start at zero, so clear it in stream order before the kernel runs.
-    cudaError_t e = cudaMemsetAsync(scratch, 0, kStatusWordsPerCall * sizeof(unsigned int), stream);
-    if (e != cudaSuccess) {
-        set_last_error("cudaMemsetAsync(scratch)", (int)e);
-        return MXFP8_ERR_CUDA;
-    }
     QuantizeArgs a = args;
     a.status = scratch;
     return launch_quantize_tma(a, sm_count, stream);

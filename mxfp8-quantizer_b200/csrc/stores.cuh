@@ -26,59 +26,56 @@ __device__ __forceinline__ void store16(uint8_t* dst, const uint4& v, const Stor
     }
 }
 
+// The 16 bytes that start at byte h (0 <= h < 16) of the 32 bytes a | b (a
+// first, little-endian).  The word choice (h / 4) is uniform over a row's
+// lanes; the byte shift is a funnel shift.
+__device__ __forceinline__ uint4 bytes_from(const uint4& a, const uint4& b, uint32_t h) {
+    const uint32_t sh = 8u * (h & 3u);
+    uint32_t w0, w1, w2, w3, w4;
+    switch (h >> 2) {
+        case 0: w0 = a.x; w1 = a.y; w2 = a.z; w3 = a.w; w4 = b.x; break;
+        case 1: w0 = a.y; w1 = a.z; w2 = a.w; w3 = b.x; w4 = b.y; break;
+        case 2: w0 = a.z; w1 = a.w; w2 = b.x; w3 = b.y; w4 = b.z; break;
+        default: w0 = a.w; w1 = b.x; w2 = b.y; w3 = b.z; w4 = b.w; break;
+    }
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
+}
+
+// Chunk c + 1 of the staging row, which lane c of the store pass needs for
+// store_row_any when its row's destination is not 4-byte aligned (lane 7's
+// is never stored: any chunk will do).
+__device__ __forceinline__ int next_chunk(int c) { return c < 7 ? c + 1 : 7; }
+
 // QU store of one row segment of the payload tile (seg bytes, a multiple of
-// 32) from the staging row `rowbuf` (16-byte chunks XOR-swizzled by `key`) to
-// dst, which may sit at any byte offset.  A 4-byte aligned dst: lane c stores
-// its own chunk v with 16/8/4-byte stores.  Otherwise the 8 lanes of the row
-// (lane c) write the aligned 16-byte chunks of the segment, one each, built
-// from 5 words read at word granularity from the staging row and
-// funnel-shifted by the remaining byte offset, so every store instruction
-// writes whole lines; the unaligned head (16 - d bytes) and tail (d bytes) go
-// out as naturally aligned 1/2/4/8-byte pieces, one per bit of their length:
-// lanes 0-3 the head's, lanes 4-7 the tail's.  No byte outside the segment is
-// written.  Measured at 8192^2 (TB/s): 8- or 4-byte aligned rows 5.6-6.1, 1-
-// or 2-byte 3.3-3.7 (byte-wide head/tail stores: 2.8; 1-byte stores at each
-// chunk's own address: 1.3).
-__device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, const uint8_t* rowbuf, uint32_t key, int seg,
-                                              int c, const StoreWindow& w, unsigned int* status) {
+// 32) to dst, which may sit at any byte offset.  Lane c (of the row's 8)
+// holds the segment's 16-byte chunk c in v.  A 4-byte aligned dst: lane c
+// stores v with 16/8/4-byte stores.  Otherwise the 8 lanes write the aligned
+// 16-byte chunks of the segment, one each (lane c the one at dst - d + 16 (c +
+// 1), built from chunk c and chunk c + 1, vn, by a byte shift that is the same
+// for the whole row), so every such store instruction writes whole lines.
+// The unaligned head (h = 16 - d bytes) and tail (d bytes) make 16 boundary
+// bytes, slot j < h the head's byte j and slot j >= h the tail's byte
+// seg - 16 + j; lane c writes slots c and c + 8 with byte stores read from
+// the staging row `rowbuf` (16-byte chunks XOR-swizzled by `key`): no branch
+// on the lane, two store instructions per row.  No byte outside the segment
+// is written.
+__device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, const uint4& vn, const uint8_t* rowbuf,
+                                              uint32_t key, int seg, int c, const StoreWindow& w,
+                                              unsigned int* status) {
     const uint32_t d = (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15);
-    auto word = [&](int i) {  // word i of the segment (i < 32)
-        return *reinterpret_cast<const uint32_t*>(rowbuf + ((((uint32_t)i >> 2) ^ key) << 4) + (i & 3) * 4);
-    };
     if ((d & 3) == 0) {  // 4-byte aligned row: each lane's own chunk v, 16/8/4-byte stores
         if (16 * c < seg) store16<true>(dst + 16 * c, v, w, status);
         return;
     }
-    uint8_t* base = dst - d;  // 16-byte aligned
-    if (16 * (c + 1) < seg) {
-        // aligned chunk c + 1 holds segment bytes [e, e + 16), e >= 1
-        const int e = 16 * (c + 1) - (int)d;
-        const int i0 = e >> 2;
-        const uint32_t sh = 8u * (uint32_t)(e & 3);
-        uint32_t x[5];
+    const int h = 16 - (int)d;
+    if (16 * (c + 1) < seg)  // aligned chunk c + 1 of dst - d: segment bytes [16 c + h, 16 c + h + 16)
+        gstore(reinterpret_cast<uint4*>(dst - d + 16 * (c + 1)), bytes_from(v, vn, (uint32_t)h), w, status);
 #pragma unroll
-        for (int k = 0; k < 5; ++k) x[k] = word((i0 + k) & 31);  // word 32 only when sh == 0 (unused)
-        gstore(reinterpret_cast<uint4*>(base + 16 * (c + 1)),
-               make_uint4(__funnelshift_r(x[0], x[1], sh), __funnelshift_r(x[1], x[2], sh),
-                          __funnelshift_r(x[2], x[3], sh), __funnelshift_r(x[3], x[4], sh)),
-               w, status);
-    }
-    // piece k = c % 4 of the head (c < 4) or the tail (c >= 4), if that bit is set
-    const int k = c & 3;
-    const uint32_t h = 16 - d;
-    const bool tail = c >= 4;
-    if (((tail ? d : h) >> k) & 1u) {
-        // head pieces grow from the start, tail pieces shrink from the boundary
-        const int off = tail ? seg - (int)d + (int)(d & ~((2u << k) - 1)) : (int)(h & ((1u << k) - 1));
-        const int i = off >> 2;
-        const uint32_t sh = 8u * (uint32_t)(off & 3);
-        const uint32_t w0 = word(i), w1 = word((i + 1) & 31), w2 = word((i + 2) & 31);
-        const uint32_t lo = __funnelshift_r(w0, w1, sh), hi = __funnelshift_r(w1, w2, sh);
-        uint8_t* q = dst + off;
-        if (k == 0) gstore(q, (unsigned char)lo, w, status);
-        else if (k == 1) gstore(reinterpret_cast<unsigned short*>(q), (unsigned short)lo, w, status);
-        else if (k == 2) gstore(reinterpret_cast<unsigned int*>(q), lo, w, status);
-        else gstore(reinterpret_cast<uint2*>(q), make_uint2(lo, hi), w, status);
+    for (int r = 0; r < 2; ++r) {
+        const int j = c + 8 * r;
+        const int o = j < h ? j : seg - 16 + j;  // segment byte of boundary slot j
+        gstore(dst + o, rowbuf[((((uint32_t)o >> 4) ^ key) << 4) | ((uint32_t)o & 15u)], w, status);
     }
 }
 

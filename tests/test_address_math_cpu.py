@@ -10,8 +10,8 @@ restated here in Python, over every alignment the kernel can meet.
    from its box row are the row's columns; the misalignment the kernel
    computes in 32-bit arithmetic equals 2 * d_f.
 2. Any-offset stores (store_row_any): a row segment of seg bytes at any
-   address is written as aligned 16-byte chunks (funnel-shifted words) plus
-   1/2/4/8-byte head and tail pieces.  Checked: every byte of the segment is
+   address is written as aligned 16-byte chunks (byte-shifted chunk pairs)
+   plus the head and tail bytes.  Checked: every byte of the segment is
    written exactly once with its value, each store is aligned to its size,
    and nothing outside the segment is touched.
 """
@@ -84,10 +84,22 @@ def funnel_r(lo, hi, sh):
     return ((hi << 32 | lo) >> sh) & 0xFFFFFFFF
 
 
+def bytes_from(a, b, h):
+    """bytes_from in stores.cuh: 16 bytes from byte h of the 32 bytes a | b,
+    a and b given as 4 little-endian words each."""
+    w = list(a) + list(b)
+    q, sh = h >> 2, 8 * (h & 3)
+    return [funnel_r(w[q + t], w[q + t + 1], sh) for t in range(4)]
+
+
 def store_row_any(dst, seg, words):
-    """The stores store_row_any issues for one row segment: (address, size, value)."""
+    """The stores store_row_any issues for one row segment: (address, size,
+    value), from the chunks each lane loads (its own and the next) and the
+    boundary bytes it reads from the staging row."""
     stores = []
     d = dst & 15
+    chunk = [words[4 * i:4 * i + 4] for i in range(8)]
+    seg_bytes = b"".join(w.to_bytes(4, "little") for w in words)
     for c in range(8):
         if d & 3 == 0:                                   # 4-byte aligned row: each lane's own chunk
             if 16 * c < seg:
@@ -97,21 +109,14 @@ def store_row_any(dst, seg, words):
                     i = (16 * c + o) // 4
                     stores.append((a + o, width, sum(words[i + t] << (32 * t) for t in range(width // 4))))
             continue
-        base = dst - d
+        v, vn = chunk[c], chunk[min(c + 1, 7)]
+        h = 16 - d
         if 16 * (c + 1) < seg:                           # aligned chunk c + 1
-            e = 16 * (c + 1) - d
-            i0, sh = e >> 2, 8 * (e & 3)
-            x = [words[(i0 + t) & 31] for t in range(5)]
-            stores.append((base + 16 * (c + 1), 16,
-                           sum(funnel_r(x[t], x[t + 1], sh) << (32 * t) for t in range(4))))
-        k, h, tail = c & 3, 16 - d, c >= 4                # head / tail pieces
-        if ((d if tail else h) >> k) & 1:
-            off = seg - d + (d & ~((2 << k) - 1)) if tail else h & ((1 << k) - 1)
-            i, sh = off >> 2, 8 * (off & 3)
-            lo = funnel_r(words[i], words[(i + 1) & 31], sh)
-            hi = funnel_r(words[(i + 1) & 31], words[(i + 2) & 31], sh)
-            n = 1 << k
-            stores.append((dst + off, n, (lo | hi << 32) & ((1 << (8 * n)) - 1)))
+            out = bytes_from(v, vn, h)
+            stores.append((dst - d + 16 * (c + 1), 16, sum(out[t] << (32 * t) for t in range(4))))
+        for j in (c, c + 8):                             # boundary slots: head bytes, then tail bytes
+            o = j if j < h else seg - 16 + j
+            stores.append((dst + o, 1, seg_bytes[o]))
     return stores
 
 
