@@ -13,8 +13,11 @@
  * Non-finite blocks follow the reference *kernel* (MXFP8_quantizer.py:170-200
  * and 473-501), whose instructions (fma.rn.f32, mul.rn.f32x2,
  * cvt.rn.satfinite.e4m3x2.f32) are restated here from their PTX ISA
- * definitions with integer arithmetic only, so the result does not depend on
- * the host's floating-point environment (rounding mode, DAZ/FTZ).
+ * definitions with integer arithmetic only, so the quantizer's result does
+ * not depend on the host's floating-point environment (rounding mode,
+ * DAZ/FTZ).  Only the dequantize restatement (oracle_dequantize) multiplies
+ * in float: an E4M3 value times a power of two, exact unless the product
+ * falls below the normal f32 range.
  *
  * Everything is plain C99 + pthreads.
  */
@@ -67,14 +70,66 @@ static uint32_t in_to_f32_bits(uint16_t v, int dtype) {
  *                 byte = (u8)e ; inverse = f32 bits ((254 - e) << 23), u32 wraparound
  * Returns the byte; *inv_bits receives the inverse-scale bit pattern.
  * ------------------------------------------------------------------------ */
+/* Significand and exponent of a finite f32 >= 0: value = *sig * 2^*exp. */
+static void f32_split(uint32_t b, uint64_t* sig, int* exp) {
+    uint32_t e = (b >> 23) & 0xFF, m = b & 0x7FFFFF;
+    if (e == 0) { *sig = m; *exp = -149; }
+    else { *sig = (uint64_t)m | 0x800000u; *exp = (int)e - 150; }
+}
+
+static int msb64(uint64_t v) { int p = -1; while (v) { v >>= 1; ++p; } return p; }
+
+/* fma.rn.f32(a, c, e) for finite a >= 0 and c, e > 0 whose result is a
+ * normal f32 (here s >= e = f32(1e-12) > 2^-126 and a <= the bf16 maximum,
+ * so it is), in integer arithmetic: the exact sum a*c + e, then one
+ * round-to-nearest-even to 24 significant bits (PTX ISA, fma.rn.f32). */
+static uint32_t fma_rn_pos_bits(uint32_t a, uint32_t c, uint32_t e) {
+    uint64_t sa, sc, se;
+    int xa, xc, xe;
+    f32_split(a, &sa, &xa);
+    f32_split(c, &sc, &xc);
+    f32_split(e, &se, &xe);
+    uint64_t s1 = sa * sc, s2 = se;  /* terms s1 * 2^x1 (the product, exact in 48 bits) and s2 * 2^x2 */
+    int x1 = xa + xc, x2 = xe;
+    if (s1 == 0) return e;
+    int p1 = msb64(s1), p2 = msb64(s2);
+    s1 <<= 62 - p1; x1 -= 62 - p1;  /* both significands now have bit 62 as their top bit */
+    s2 <<= 62 - p2; x2 -= 62 - p2;
+    if (x2 > x1) { uint64_t ts = s1; s1 = s2; s2 = ts; int tx = x1; x1 = x2; x2 = tx; }
+    const int k = x1 - x2;  /* align the smaller term under the larger one, 64 bits below it */
+    unsigned __int128 acc = (unsigned __int128)s1 << 64;
+    int sticky = 0;
+    if (k <= 64) {
+        acc += (unsigned __int128)s2 << (64 - k);
+    } else if (k < 127) {
+        acc += s2 >> (k - 64);
+        sticky = (s2 & ((1ull << (k - 64)) - 1)) != 0;
+    } else {
+        sticky = 1;
+    }
+    /* value = acc * 2^(x1 - 64), acc's top bit at 126 or 127 */
+    const int top = (acc >> 127) ? 127 : 126;
+    const int drop = top - 23;  /* bits below the 24-bit significand */
+    uint64_t sig = (uint64_t)(acc >> drop);
+    const unsigned __int128 rest = acc & (((unsigned __int128)1 << drop) - 1);
+    const unsigned __int128 half = (unsigned __int128)1 << (drop - 1);
+    int exp = top + x1 - 64;  /* unbiased exponent of the leading bit */
+    if (rest > half || (rest == half && (sticky || (sig & 1))) ) sig += 1;
+    if (sig >> 24) { sig >>= 1; exp += 1; }
+    return ((uint32_t)(exp + 127) << 23) | ((uint32_t)sig & 0x7FFFFFu);
+}
+
 uint8_t oracle_scale_from_amax_bits(uint16_t amax_bits, int dtype, uint32_t* inv_bits) {
     uint32_t e;
     if ((amax_bits & 0x7FFF) == 0) {
         e = 127u;
     } else {
-        float amax = f32_from_bits(in_to_f32_bits(amax_bits & 0x7FFF, dtype));
-        float s = fmaf(amax, f32_from_bits(INV_448_BITS), f32_from_bits(EPS_BITS));
-        uint32_t b = bits_from_f32(s);
+        const uint32_t a = in_to_f32_bits(amax_bits & 0x7FFF, dtype);
+        uint32_t b;
+        if ((a & 0x7F800000u) == 0x7F800000u)
+            b = (a & 0x7FFFFFu) ? 0x7FFFFFFFu : 0x7F800000u;  /* NaN stays NaN, inf * c + e = inf */
+        else
+            b = fma_rn_pos_bits(a, INV_448_BITS, EPS_BITS);
         e = (b >> 23) & 0xFFu;
         if (b & 0x7FFFFFu) e += 1u;
     }
