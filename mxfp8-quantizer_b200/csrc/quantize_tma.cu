@@ -50,7 +50,9 @@
 //
 // Outputs at any offset (template flag QU, when Q, ld_q or S is not 16-byte
 // aligned): the store pass writes Q rows through store_row_any and the scale
-// chunk with 16/8/4-byte stores (S is at least 4-byte aligned).
+// chunk with 16/8/4-byte stores (S is at least 4-byte aligned).  Realigning
+// rows costs instructions, so these kernels run 2 CTAs per SM with 2 stages
+// each, as the row path does, for twice the warps to hide them.
 //
 // Reference behaviour restated (not its structure): MXFP8_quantizer.py:355-525.
 #include <cuda.h>
@@ -114,7 +116,7 @@ __device__ __forceinline__ void prefetch_tile(const XMaps<ROWS>& xm, const TmaPa
 }
 
 template <int DT, int STAGES, bool ROWS, bool QU>
-__global__ void __launch_bounds__(kThreads, ROWS ? kRowCtasPerSm : 1)
+__global__ void __launch_bounds__(kThreads, (ROWS || QU) ? kRowCtasPerSm : 1)
     quantize_tma_kernel(const __grid_constant__ XMaps<ROWS> xm, const TmaParams p) {
     using L = Layout<STAGES, ROWS>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -389,8 +391,8 @@ static int encode_x_maps(const QuantizeArgs& a, XMaps<ROWS>& xm) {
 
 template <int DT, bool ROWS, bool QU>
 static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
-    constexpr int kSt = ROWS ? kRowStages : kStages;
-    constexpr int kCtasPerSm = ROWS ? kRowCtasPerSm : 1;
+    constexpr int kSt = (ROWS || QU) ? kRowStages : kStages;
+    constexpr int kCtasPerSm = (ROWS || QU) ? kRowCtasPerSm : 1;
     using L = Layout<kSt, ROWS>;
     auto kernel = quantize_tma_kernel<DT, kSt, ROWS, QU>;
     // The shared-memory opt-in is per device: set it once per device, so that
@@ -401,7 +403,7 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
     const uint64_t bit = 1ull << (dev & 63);
     if (e == cudaSuccess && !(attr_set.load(std::memory_order_acquire) & bit)) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::alloc);
-        if (e == cudaSuccess && ROWS)  // room for kRowCtasPerSm CTAs
+        if (e == cudaSuccess && (ROWS || QU))
             e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared);
         if (e == cudaSuccess) attr_set.fetch_or(bit, std::memory_order_acq_rel);
