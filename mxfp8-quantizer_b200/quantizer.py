@@ -219,10 +219,17 @@ class HostQuantizer:
     directions and the kernel overlap.  Device staging buffers are allocated
     once here.  Pass pinned host tensors; pageable ones still work but do
     not overlap.  The output geometry is the tight one, (m, ceil(k/32)*32).
-    On a B200 with PCIe Gen5 (55 GB/s each way) an 8192x8192 bf16 call takes
-    2.67 ms at 512-row chunks against 2.56 ms for the two copies alone."""
 
-    def __init__(self, m: int, k: int, dtype: torch.dtype = torch.bfloat16, device=None, chunk_rows: int = 512):
+    With pinned host tensors the pipeline (about 50 copies, launches and
+    stream joins for 8192 rows) is captured once into a CUDA graph per set of
+    host buffers and replayed on later calls, so a call costs one graph
+    launch of host time instead of tens of microseconds of Python per chunk;
+    the first call with new buffers runs eagerly and captures.  On a B200
+    with PCIe Gen5 an 8192x8192 bf16 call takes 2.70-2.75 ms against 2.55-2.58
+    ms for the same bytes copied in both directions at once with no kernel."""
+
+    def __init__(self, m: int, k: int, dtype: torch.dtype = torch.bfloat16, device=None, chunk_rows: int = 512,
+                 use_graph: bool = True):
         if chunk_rows % SCALE_ROWS_PER_PACK or chunk_rows <= 0:
             raise ValueError("chunk_rows must be a positive multiple of 128")
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -236,8 +243,11 @@ class HostQuantizer:
         self.streams = [torch.cuda.Stream(self.device) for _ in range(3)]
         self.chunks = [(r0, min(m, r0 + chunk_rows)) for r0 in range(0, m, chunk_rows)]
         self.launches_per_call = len(self.chunks)
+        self.use_graph = use_graph
+        self._graph = None
+        self._graph_key = None
 
-    def __call__(self, x_host: torch.Tensor, q_host: torch.Tensor, s_host: torch.Tensor) -> None:
+    def _enqueue(self, x_host: torch.Tensor, q_host: torch.Tensor, s_host: torch.Tensor) -> None:
         h2d, comp, d2h = self.streams
         cur = torch.cuda.current_stream(self.device)
         start = torch.cuda.Event()
@@ -263,9 +273,30 @@ class HostQuantizer:
             with torch.cuda.stream(d2h):
                 q_host[r0:r1].copy_(self.q[r0:r1], non_blocking=True)
                 s_host[s0:s0 + s_len].copy_(self.s[s0:s0 + s_len], non_blocking=True)
-        end = torch.cuda.Event()
-        end.record(d2h)
-        cur.wait_event(end)
+        for st in self.streams:  # join every stream back (a captured fork must rejoin its origin)
+            end = torch.cuda.Event()
+            end.record(st)
+            cur.wait_event(end)
+
+    def __call__(self, x_host: torch.Tensor, q_host: torch.Tensor, s_host: torch.Tensor) -> None:
+        pinned = x_host.is_pinned() and q_host.is_pinned() and s_host.is_pinned()
+        if not (self.use_graph and pinned):
+            self._enqueue(x_host, q_host, s_host)
+            return
+        key = tuple((t.data_ptr(), tuple(t.shape), t.dtype) for t in (x_host, q_host, s_host))
+        if self._graph is not None and key == self._graph_key:
+            with torch.cuda.device(self.device):
+                self._graph.replay()
+            return
+        # New buffers: this call runs eagerly (it also makes the library's
+        # first call on the device, which allocates, before any capture),
+        # then the same pipeline is captured for the calls that follow.
+        self._enqueue(x_host, q_host, s_host)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.device(self.device):
+            with torch.cuda.graph(graph):
+                self._enqueue(x_host, q_host, s_host)
+        self._graph, self._graph_key = graph, key
 
 
 class CompiledQuantizer:

@@ -336,17 +336,20 @@ def test_bounded_wait_times_out_and_reports(capi, golden):
     assert sha(q) == golden["cases"]["c1"]["q_sha256"] and sha(s) == golden["cases"]["c1"]["s_sha256"]
 
 
+@pytest.mark.parametrize("use_graph", [True, False])
 @pytest.mark.parametrize("m,k,dtype", [(2500, 1000, "fp16"), (1300, 777, "bf16")])
-def test_host_quantizer_matches_device_path(m, k, dtype, capi, oracle_mod):
+def test_host_quantizer_matches_device_path(m, k, dtype, use_graph, capi, oracle_mod):
     """HostQuantizer (pinned host X in, host Q/S out, row chunks over three
-    streams) gives the bytes of the device path, for a ragged row count; odd
-    K takes the device's per-phase tensor-map path."""
+    streams, replayed from a CUDA graph or enqueued eagerly) gives the bytes
+    of the device path, for a ragged row count; odd K takes the device's
+    per-phase tensor-map path."""
     import MXFP8_quantizer
 
     pkg = MXFP8_quantizer.load_package()
     bits = inputs.normal(m, k, 55, dtype, sigma=4.0)
     x_host = inputs.bits_to_torch(bits, dtype).pin_memory()
-    hq = pkg.HostQuantizer(m, k, torch.float16 if dtype == "fp16" else torch.bfloat16, chunk_rows=512)
+    hq = pkg.HostQuantizer(m, k, torch.float16 if dtype == "fp16" else torch.bfloat16, chunk_rows=512,
+                           use_graph=use_graph)
     q_host = torch.empty((m, hq.q_cols), dtype=torch.uint8).pin_memory()
     s_host = torch.empty((hq.s_bytes,), dtype=torch.uint8).pin_memory()
     for _ in range(2):
@@ -355,6 +358,37 @@ def test_host_quantizer_matches_device_path(m, k, dtype, capi, oracle_mod):
     q_ref, s_ref = oracle_mod.quantize(bits, dtype, m, hq.q_cols)
     assert np.array_equal(q_host.numpy(), q_ref)
     assert np.array_equal(s_host.numpy(), s_ref)
+
+
+def test_host_quantizer_graph_replays_read_the_buffers_anew(capi, oracle_mod):
+    """A replayed call copies whatever the pinned X holds now (new values in
+    the same buffer give their own Q and S), and new buffers are captured
+    afresh."""
+    import MXFP8_quantizer
+
+    pkg = MXFP8_quantizer.load_package()
+    m, k = 1100, 2048
+    hq = pkg.HostQuantizer(m, k, torch.bfloat16, chunk_rows=256)
+    x_host = torch.empty((m, k), dtype=torch.bfloat16).pin_memory()
+    q_host = torch.empty((m, hq.q_cols), dtype=torch.uint8).pin_memory()
+    s_host = torch.empty((hq.s_bytes,), dtype=torch.uint8).pin_memory()
+    for seed in (61, 62, 63):  # eager + capture, then two replays with new values
+        bits = inputs.normal(m, k, seed, "bf16", sigma=3.0)
+        x_host.copy_(inputs.bits_to_torch(bits, "bf16"))
+        hq(x_host, q_host, s_host)
+        torch.cuda.synchronize()
+        q_ref, s_ref = oracle_mod.quantize(bits, "bf16", m, hq.q_cols)
+        assert np.array_equal(q_host.numpy(), q_ref) and np.array_equal(s_host.numpy(), s_ref), seed
+    bits = inputs.normal(m, k, 64, "bf16")
+    x2 = inputs.bits_to_torch(bits, "bf16").pin_memory()
+    q2 = torch.zeros_like(q_host).pin_memory()
+    s2 = torch.zeros_like(s_host).pin_memory()
+    for _ in range(2):
+        hq(x2, q2, s2)
+    torch.cuda.synchronize()
+    q_ref, s_ref = oracle_mod.quantize(bits, "bf16", m, hq.q_cols)
+    assert np.array_equal(q2.numpy(), q_ref) and np.array_equal(s2.numpy(), s_ref)
+    assert capi.device_status(clear=True) == 0
 
 
 def test_dequantize_unaligned_output_rows(capi, oracle_mod):
