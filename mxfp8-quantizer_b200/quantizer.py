@@ -246,6 +246,7 @@ class HostQuantizer:
         self.use_graph = use_graph
         self._graph = None
         self._graph_key = None
+        self._capture_stream = torch.cuda.Stream(self.device) if use_graph else None
 
     def _enqueue(self, x_host: torch.Tensor, q_host: torch.Tensor, s_host: torch.Tensor) -> None:
         h2d, comp, d2h = self.streams
@@ -291,10 +292,13 @@ class HostQuantizer:
         # New buffers: this call runs eagerly (it also makes the library's
         # first call on the device, which allocates, before any capture),
         # then the same pipeline is captured for the calls that follow.
+        # The capture is thread-local: other threads of the process (a
+        # process group's watchdog polling its events, for one) may keep
+        # making CUDA calls meanwhile.
         self._enqueue(x_host, q_host, s_host)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.device(self.device):
-            with torch.cuda.graph(graph):
+            with torch.cuda.graph(graph, stream=self._capture_stream, capture_error_mode="thread_local"):
                 self._enqueue(x_host, q_host, s_host)
         self._graph, self._graph_key = graph, key
 

@@ -13,7 +13,7 @@ libmxfp8.so and go unmodified into the reference's vendored CUTLASS GEMM
 (blockscaled_gemm.py, ``Sm100BlockScaledPersistentDenseGemmKernel`` +
 ``scaled_mm``), whose fp32 C the reference compares with an fp32 GEMM of the
 dequantized operands (rtol = atol = 1e-2).  Only the suite rows with a 1x1
-cluster run (no cluster multicast anywhere); one B200.  The published errors
+cluster run (one CTA per cluster); one B200.  The published errors
 for these rows are README.md:164 and README.md:169 of the reference.
 Needs a B200, CuTeDSL and the reference's two files; nothing else reads the
 reference at run time.
