@@ -55,15 +55,16 @@ def algo_bytes(m: int, k: int) -> int:
     return 2 * m * k + m * k + m * (k // SCALE_VEC)
 
 
-def launches_per_call(m: int, k: int, ld_x: int) -> int:
+def launches_per_call(m: int, k: int, ld_x: int, q_any_offset: bool = False) -> int:
     """Kernel launches one mxfp8_quantize call makes: the pipelined kernel
     splits problems of more than 148*128 tiles (148*64 on its unaligned-row
-    path) into launches of whole 128-row tiles, mirroring kMaxTilesPerLaunch
-    and kMaxTilesPerLaunchRows in csrc/quantize_tma.cu.  X is assumed
-    16-byte aligned (torch allocations are)."""
+    path and its any-offset store path, which run two CTAs per SM) into
+    launches of whole 128-row tiles, mirroring kMaxTilesPerLaunch and
+    kMaxTilesPerLaunchRows in csrc/quantize_tma.cu.  X is assumed 16-byte
+    aligned (torch allocations are)."""
     col_tiles = -(-(-(-k // SCALE_VEC)) // 4)
     row_tiles = -(-m // 128)
-    max_tiles = 148 * 128 if ld_x % 8 == 0 else 148 * 64
+    max_tiles = 148 * 128 if ld_x % 8 == 0 and not q_any_offset else 148 * 64
     rows_per_launch = max(1, max_tiles // col_tiles) if row_tiles * col_tiles > max_tiles else row_tiles
     return -(-row_tiles // rows_per_launch)
 
@@ -840,7 +841,7 @@ def main() -> None:
                                          "directions at once, no kernel"},
                 "frac_of_copy_ceiling": e2e_value / ceiling_value,
                 "host_cpus": numa_cpus or "unchanged"},
-        "gpu_launches": args.steps * launches_per_call(m, k, k),
+        "gpu_launches": args.steps * launches_per_call(m, k, k, q_any_offset=args.q_offset % 16 != 0),
         "verification": ver,
     })
     if c5 is not None:

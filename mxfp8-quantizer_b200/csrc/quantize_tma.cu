@@ -115,7 +115,7 @@ __device__ __forceinline__ void prefetch_tile(const XMaps<ROWS>& xm, const TmaPa
     }
 }
 
-template <int DT, int STAGES, bool ROWS, bool QU>
+template <int DT, int STAGES, bool ROWS, bool QU, int QW>
 __global__ void __launch_bounds__(kThreads, (ROWS || QU) ? kRowCtasPerSm : 1)
     quantize_tma_kernel(const __grid_constant__ XMaps<ROWS> xm, const TmaParams p) {
     using L = Layout<STAGES, ROWS>;
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, (ROWS || QU) ? kRowCtasPerSm : 1)
                     uint4 vn = v;
                     if (reinterpret_cast<uintptr_t>(dst) & 3)  // realigned row: the next chunk too
                         vn = *reinterpret_cast<const uint4*>(srow + ((next_chunk(chunk) ^ key) << 4));
-                    if (grow < p.q_rows) store_row_any(dst, v, vn, srow, key, seg, chunk, p.qw, p.status);
+                    if (grow < p.q_rows) store_row_any<QW>(dst, v, vn, srow, key, seg, chunk, p.qw, p.status);
                 } else {
                     const int col = ct * kTileCols + chunk * 16;  // q_cols % 32 == 0: a chunk is all in or all out
                     if (grow < p.q_rows && col < p.q_cols)
@@ -299,9 +299,11 @@ __global__ void __launch_bounds__(kThreads, (ROWS || QU) ? kRowCtasPerSm : 1)
 
 constexpr int kStages = 3;
 constexpr int64_t kMaxTilesPerLaunch = 148 * 128;  // ~0.94 GB of traffic per launch
-// The row path's two CTAs per SM drift apart sooner: above ~8k tiles its
-// launch times turned bimodal (16384 x 16383: min 6.43, median 5.68 TB/s);
-// split at 148 x 64 tiles, median 6.40, no change at 8192 tiles or below.
+// The two-CTA-per-SM kernels (the row path, the any-offset stores) drift
+// apart sooner: above ~8k tiles their launch times turned bimodal (16384 x
+// 16383: min 6.43, median 5.68 TB/s; 16384^2 with Q 1 byte off: 4.81 or
+// 5.51 from call to call); split at 148 x 64 tiles, median 6.40 on the row
+// path, no change at 8192 tiles or below.
 constexpr int64_t kMaxTilesPerLaunchRows = 148 * 64;
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -389,12 +391,12 @@ static int encode_x_maps(const QuantizeArgs& a, XMaps<ROWS>& xm) {
     }
 }
 
-template <int DT, bool ROWS, bool QU>
+template <int DT, bool ROWS, bool QU, int QW = -1>
 static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
     constexpr int kSt = (ROWS || QU) ? kRowStages : kStages;
     constexpr int kCtasPerSm = (ROWS || QU) ? kRowCtasPerSm : 1;
     using L = Layout<kSt, ROWS>;
-    auto kernel = quantize_tma_kernel<DT, kSt, ROWS, QU>;
+    auto kernel = quantize_tma_kernel<DT, kSt, ROWS, QU, QW>;
     // The shared-memory opt-in is per device: set it once per device, so that
     // later launches (including ones under stream capture) make no such call.
     static std::atomic<uint64_t> attr_set{0};
@@ -440,7 +442,7 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
     // in step every ~0.9 GB measured 6.77 vs 6.35 TB/s at 131072x16384 and
     // changed nothing at 16384^2 or below.
     int64_t rows_per_launch = n_row_tiles;
-    const int64_t max_tiles = ROWS ? kMaxTilesPerLaunchRows : kMaxTilesPerLaunch;
+    const int64_t max_tiles = (ROWS || QU) ? kMaxTilesPerLaunchRows : kMaxTilesPerLaunch;
     if (n_row_tiles * a.col_chunks > max_tiles) {
         rows_per_launch = max_tiles / a.col_chunks;
         if (rows_per_launch < 1) rows_per_launch = 1;
@@ -471,6 +473,24 @@ static int launch_tma_typed(const QuantizeArgs& a, int sm_count, cudaStream_t st
     return MXFP8_OK;
 }
 
+// Any-offset stores with X through one tensor map.  When every Q row starts
+// at the same byte offset d within 16 bytes (ld_q % 16 == 0) and d is not a
+// multiple of 4, every realigned row takes its words from the same place
+// (h / 4 with h = 16 - d), so a kernel with that word offset built in runs
+// without the per-row selects: 8192^2 bf16 with Q 1 byte off, 5.33 -> 5.51
+// TB/s (every offset 1-15 that is not a multiple of 4: 5.49-5.51).
+template <int DT>
+static int launch_tensor_qu(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
+    const uint32_t d = (uint32_t)(reinterpret_cast<uintptr_t>(a.q) & 15);
+    if (a.ld_q % 16 != 0 || (d & 3) == 0) return launch_tma_typed<DT, false, true>(a, sm_count, stream);
+    switch ((16 - d) >> 2) {
+        case 0: return launch_tma_typed<DT, false, true, 0>(a, sm_count, stream);
+        case 1: return launch_tma_typed<DT, false, true, 1>(a, sm_count, stream);
+        case 2: return launch_tma_typed<DT, false, true, 2>(a, sm_count, stream);
+        default: return launch_tma_typed<DT, false, true, 3>(a, sm_count, stream);
+    }
+}
+
 int launch_quantize_tma(const QuantizeArgs& a, int sm_count, cudaStream_t stream) {
     // rows a single tensor map can describe: 16-byte aligned base and row stride
     const bool tensor = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.ld_x % 8 == 0;
@@ -479,13 +499,13 @@ int launch_quantize_tma(const QuantizeArgs& a, int sm_count, cudaStream_t stream
                     (reinterpret_cast<uintptr_t>(a.s) & 15) != 0;
     if (a.dtype == kBF16) {
         if (qu)
-            return tensor ? launch_tma_typed<kBF16, false, true>(a, sm_count, stream)
+            return tensor ? launch_tensor_qu<kBF16>(a, sm_count, stream)
                           : launch_tma_typed<kBF16, true, true>(a, sm_count, stream);
         return tensor ? launch_tma_typed<kBF16, false, false>(a, sm_count, stream)
                       : launch_tma_typed<kBF16, true, false>(a, sm_count, stream);
     }
     if (qu)
-        return tensor ? launch_tma_typed<kFP16, false, true>(a, sm_count, stream)
+        return tensor ? launch_tensor_qu<kFP16>(a, sm_count, stream)
                       : launch_tma_typed<kFP16, true, true>(a, sm_count, stream);
     return tensor ? launch_tma_typed<kFP16, false, false>(a, sm_count, stream)
                   : launch_tma_typed<kFP16, true, false>(a, sm_count, stream);

@@ -27,15 +27,24 @@ __device__ __forceinline__ void store16(uint8_t* dst, const uint4& v, const Stor
 }
 
 // The 16 bytes that start at byte h (0 <= h < 16) of the 32 bytes a | b (a
-// first, little-endian): words h / 4 .. h / 4 + 4 chosen by two levels of
-// selects (no branch; a switch measured 4.65 vs 4.87 TB/s at a 1-byte Q
-// offset), then a funnel shift by the remaining bytes.
+// first, little-endian): words h / 4 .. h / 4 + 4, then a funnel shift by
+// the remaining bytes.  QW >= 0: the caller knows h / 4 == QW for every row
+// (all Q rows at the same 16-byte phase), so the words are fixed at compile
+// time.  QW < 0: the words are picked with two levels of selects (no branch;
+// a switch measured 4.65 vs 4.87 TB/s at a 1-byte Q offset).
+template <int QW>
 __device__ __forceinline__ uint4 bytes_from(const uint4& a, const uint4& b, uint32_t h) {
     const uint32_t sh = 8u * (h & 3u);
-    const bool b0 = (h & 4u) != 0, b1 = (h & 8u) != 0;
-    const uint32_t t0 = b0 ? a.y : a.x, t1 = b0 ? a.z : a.y, t2 = b0 ? a.w : a.z, t3 = b0 ? b.x : a.w,
-                   t4 = b0 ? b.y : b.x, t5 = b0 ? b.z : b.y, t6 = b0 ? b.w : b.z;
-    const uint32_t w0 = b1 ? t2 : t0, w1 = b1 ? t3 : t1, w2 = b1 ? t4 : t2, w3 = b1 ? t5 : t3, w4 = b1 ? t6 : t4;
+    uint32_t w0, w1, w2, w3, w4;
+    if constexpr (QW >= 0) {
+        const uint32_t W[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        w0 = W[QW]; w1 = W[QW + 1]; w2 = W[QW + 2]; w3 = W[QW + 3]; w4 = W[QW + 4];
+    } else {
+        const bool b0 = (h & 4u) != 0, b1 = (h & 8u) != 0;
+        const uint32_t t0 = b0 ? a.y : a.x, t1 = b0 ? a.z : a.y, t2 = b0 ? a.w : a.z, t3 = b0 ? b.x : a.w,
+                       t4 = b0 ? b.y : b.x, t5 = b0 ? b.z : b.y, t6 = b0 ? b.w : b.z;
+        w0 = b1 ? t2 : t0; w1 = b1 ? t3 : t1; w2 = b1 ? t4 : t2; w3 = b1 ? t5 : t3; w4 = b1 ? t6 : t4;
+    }
     return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
                       __funnelshift_r(w3, w4, sh));
 }
@@ -58,6 +67,7 @@ __device__ __forceinline__ int next_chunk(int c) { return c < 7 ? c + 1 : 7; }
 // the staging row `rowbuf` (16-byte chunks XOR-swizzled by `key`): no branch
 // on the lane, two store instructions per row.  No byte outside the segment
 // is written.
+template <int QW>
 __device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, const uint4& vn, const uint8_t* rowbuf,
                                               uint32_t key, int seg, int c, const StoreWindow& w,
                                               unsigned int* status) {
@@ -68,7 +78,7 @@ __device__ __forceinline__ void store_row_any(uint8_t* dst, const uint4& v, cons
     }
     const int h = 16 - (int)d;
     if (16 * (c + 1) < seg)  // aligned chunk c + 1 of dst - d: segment bytes [16 c + h, 16 c + h + 16)
-        gstore(reinterpret_cast<uint4*>(dst - d + 16 * (c + 1)), bytes_from(v, vn, (uint32_t)h), w, status);
+        gstore(reinterpret_cast<uint4*>(dst - d + 16 * (c + 1)), bytes_from<QW>(v, vn, (uint32_t)h), w, status);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int j = c + 8 * r;

@@ -54,3 +54,7 @@ def test_launches_per_call_follows_the_split_rule():
     assert bench.launches_per_call(38000, 8192, 8192) == 2
     assert bench.launches_per_call(38000, 8191, 8191) == 3
     assert bench.launches_per_call(1, 65535 * 256, 65535 * 256) == 1
+    # Q at any offset: the two-CTA split too
+    assert bench.launches_per_call(8192, 8192, 8192, q_any_offset=True) == 1
+    assert bench.launches_per_call(16384, 16384, 16384, q_any_offset=True) == 2
+    assert bench.launches_per_call(38000, 8192, 8192, q_any_offset=True) == 3

@@ -513,8 +513,9 @@ def test_extreme_aspect_ratios(m, k, dtype, geometry, capi, oracle_mod):
         check_against_oracle(capi, oracle_mod, bits, dtype, m, (k + 31) // 32 * 32)
 
 
-@pytest.mark.parametrize("m,k", [(8192, 8192), (38000, 8192), (38000, 8191), (16384, 16383)])
-def test_launch_count_matches_bench_accounting(m, k, capi):
+@pytest.mark.parametrize("m,k,q_offset", [(8192, 8192, 0), (38000, 8192, 0), (38000, 8191, 0), (16384, 16383, 0),
+                                          (16384, 16384, 1), (38000, 8192, 8)])
+def test_launch_count_matches_bench_accounting(m, k, q_offset, capi):
     """The kernel launches one call makes, counted by the CUDA profiler,
     equal bench.py's gpu_launches rule (the launch split by tile count)."""
     import bench
@@ -523,25 +524,26 @@ def test_launch_count_matches_bench_accounting(m, k, capi):
     q_cols = (k + 31) // 32 * 32
     s_bytes = capi.scale_storage_bytes(m, q_cols)
     x = torch.zeros((m, k), dtype=torch.bfloat16, device="cuda")
-    q = torch.empty((m, q_cols), dtype=torch.uint8, device="cuda")
+    q = torch.empty((m * q_cols + 16,), dtype=torch.uint8, device="cuda")
     s = torch.empty((s_bytes,), dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    args = (x.data_ptr(), 0, m, k, k, q.data_ptr(), m, q_cols, q_cols, s.data_ptr(), s_bytes, stream)
+    args = (x.data_ptr(), 0, m, k, k, q.data_ptr() + q_offset, m, q_cols, q_cols, s.data_ptr(), s_bytes, stream)
     capi.quantize(*args)
     torch.cuda.synchronize()
     with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
         capi.quantize(*args)
         torch.cuda.synchronize()
     launches = sum(1 for e in prof.events() if "quantize_tma_kernel" in e.name)
-    assert launches == bench.launches_per_call(m, k, k)
+    assert launches == bench.launches_per_call(m, k, k, q_any_offset=q_offset % 16 != 0)
 
 
 def test_three_paths_agree_across_launch_split(capi):
     """38000 x 8191 bf16 (622 MB): the same X through the row path (row
     stride 8191, three launches of 148 + 148 + 1 row tiles), the tensor path
     (row stride 8192, two launches of 296 + 1 row tiles) and the tensor path
-    with Q 8 bytes off 16-byte alignment (narrower stores) gives identical Q
-    and S bytes, in the reference geometry."""
+    with Q 8 bytes off 16-byte alignment (narrower stores, three launches
+    like the row path) gives identical Q and S bytes, in the reference
+    geometry."""
     m, k = 38000, 8191
     q_rows, q_cols = (m + 7) // 8 * 8, (k + 255) // 256 * 256
     s_bytes = capi.scale_storage_bytes(q_rows, q_cols)
@@ -603,6 +605,18 @@ def test_randomized_output_layouts(capi, oracle_mod):
             kw.update(ld_x=k + int(rng.integers(0, 9)), x_offset=int(rng.integers(0, 8)))
         bits = inputs.normal(m, k, 5000 + case, dtype, sigma=float(10 ** rng.uniform(-2, 2)))
         check_against_oracle(capi, oracle_mod, bits, dtype, m, q_cols, **kw)
+
+
+@pytest.mark.parametrize("q_offset", range(16))
+def test_every_q_offset_with_rows_in_phase(q_offset, capi, oracle_mod):
+    """Q at each byte offset within 16 bytes with ld_q % 16 == 0, so every row
+    starts at the same offset: the any-offset kernels with the word offset
+    built in (offsets 1-3, 5-7, 9-11, 13-15), the 4-byte-aligned rows (4, 8,
+    12) and the aligned path (0), ragged M and K, S at a 4-byte offset."""
+    dtype = "bf16" if q_offset % 2 else "fp16"
+    bits = inputs.normal(300, 1000, 700 + q_offset, dtype, sigma=7.0)
+    check_against_oracle(capi, oracle_mod, bits, dtype, 300, 1024, q_offset=q_offset, ld_q=1024 + 16 * (q_offset % 3),
+                         s_offset=4 * (q_offset % 4))
 
 
 def test_randomized_shapes_layouts_and_values(capi, oracle_mod):
