@@ -802,6 +802,7 @@ def main() -> None:
     c5 = None
     if not args.no_c5 and args.m == M_DEFAULT and args.k == K_DEFAULT and args.q_offset == 0:
         c5 = run_c5(args, pkg, rank, world, dev, barrier, sampler, max(3, min(args.steps, 200)))
+    sampler.close()  # no GPU work below; the CPU baselines get every host thread
 
     cpu = cpu_torch = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -818,7 +819,6 @@ def main() -> None:
                      "sample": f"{torch_rows}x{k} rows of the workload, best of 3, the recipe as torch CPU tensor "
                                f"code (reference_quantize) incl. scale packing"}
 
-    sampler.close()
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
